@@ -1,0 +1,616 @@
+// Persistent tcgen05 implicit-GEMM kernel (sm_100a) for RefineNet / ScoreNet.
+//
+// One CTA per SM walks output tiles of 128 rows x BN channels. Warp roles:
+//   warp 0     producer: per 64-channel chunk, one bulk copy per channel plane
+//              brings a window of 128 + span rows of the activation into shared
+//              memory (reused by every tap of the convolution); per 64-wide K
+//              stage a TMA tile load brings the weights (128B swizzle).
+//   warp 1     MMA issuer (one lane) + TMEM owner: tcgen05.mma kind::f16,
+//              M=128, N=BN, K=16, fp32 accumulators in TMEM, two accumulator
+//              buffers so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   warps 2-5  epilogue: tcgen05.ld rows of the accumulator, bias / residual /
+//              positional embedding / ReLU, bf16|fp16 stores into the KP8
+//              destination layout chosen by the layer (see include/fpk.h).
+// The activation window uses the no-swizzle K-major core-matrix layout
+// [plane][row][16 B]; shifting a convolution tap by one row is a 16-byte move of
+// the descriptor start address, so all taps read the same staged window.
+// Every mbarrier wait is bounded: on timeout the kernel records an error code
+// in desc.error_flag and all roles drain and exit.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <type_traits>
+#include <unordered_map>
+
+#include "fpk.h"
+
+namespace fpb {
+
+int fail(const std::string& msg);
+int checkLaunch(const char* what);
+
+namespace gemm {
+
+constexpr int kThreads = 192;
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 64;  // elements per weight stage (128 bytes of bf16/fp16)
+constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+struct Smem {
+  uint64_t a_full[2], a_empty[2];
+  uint64_t b_full[8], b_empty[8];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint32_t smemU32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbarInit(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smemU32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbarExpectTx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smemU32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbarArrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemU32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbarTryWait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smemU32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and records `code`) after ~2 s or when another
+// role already reported an error.
+__device__ __noinline__ bool waitBar(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const long long start = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbarTryWait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (clock64() - start > kTimeoutCycles) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// Drain wait used on exit paths: bounded, ignores the error flag.
+__device__ __noinline__ void drainBar(uint64_t* bar, uint32_t parity) {
+  const long long start = clock64();
+  while (!mbarTryWait(bar, parity)) {
+    if (clock64() - start > kTimeoutCycles) return;
+  }
+}
+
+__device__ __forceinline__ void bulkCopy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smemU32(dst)),
+      "l"(src), "r"(bytes), "r"(smemU32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmaLoad2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4}], [%2];" ::"r"(smemU32(dst)),
+      "l"(map), "r"(smemU32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tcFenceBefore() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tcFenceAfter() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tcCommit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smemU32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tcMma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                      uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+#define FPB_TMEM_LD32(taddr, r)                                                                  \
+  asm volatile(                                                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "    \
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "    \
+      "%28, %29, %30, %31}, [%32];"                                                              \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),      \
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),  \
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),            \
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),            \
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])             \
+      : "r"(taddr))
+
+__device__ __forceinline__ void tmemWaitLd() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05): start, leading (K-direction) and
+// stride (M/N-direction) byte offsets, descriptor version 1, layout type.
+__device__ __forceinline__ uint64_t smemDesc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                             uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
+  return d;
+}
+
+constexpr uint32_t kLayoutNone = 0;
+constexpr uint32_t kLayoutSw128 = 2;
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B K-major.
+__host__ __device__ constexpr uint32_t instrDesc(int bn, bool bf16) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(kBlockM >> 4) << 24);
+}
+
+struct Plan {
+  int cw;            // channels per chunk (32 or 64)
+  int planes;        // planes per chunk = cw / 8
+  int n_chunks;      // cin / cw
+  int stages_per_chunk;
+  int min_off, win_rows;
+  int b_stages;
+  int m_tiles, n_tiles;
+  uint32_t a_win_bytes;  // per slot
+  uint32_t b_stage_bytes;
+};
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* v);
+template <>
+__device__ __forceinline__ uint4 pack8<__nv_bfloat16>(const float* v) {
+  uint4 o;
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+  __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]);
+  __nv_bfloat162 h3 = __floats2bfloat162_rn(v[6], v[7]);
+  o.x = *reinterpret_cast<uint32_t*>(&h0);
+  o.y = *reinterpret_cast<uint32_t*>(&h1);
+  o.z = *reinterpret_cast<uint32_t*>(&h2);
+  o.w = *reinterpret_cast<uint32_t*>(&h3);
+  return o;
+}
+template <>
+__device__ __forceinline__ uint4 pack8<__half>(const float* v) {
+  uint4 o;
+  __half2 h0 = __floats2half2_rn(v[0], v[1]);
+  __half2 h1 = __floats2half2_rn(v[2], v[3]);
+  __half2 h2 = __floats2half2_rn(v[4], v[5]);
+  __half2 h3 = __floats2half2_rn(v[6], v[7]);
+  o.x = *reinterpret_cast<uint32_t*>(&h0);
+  o.y = *reinterpret_cast<uint32_t*>(&h1);
+  o.z = *reinterpret_cast<uint32_t*>(&h2);
+  o.w = *reinterpret_cast<uint32_t*>(&h3);
+  return o;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(uint4 u, float* v);
+template <>
+__device__ __forceinline__ void unpack8<__nv_bfloat16>(uint4 u, float* v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void unpack8<__half>(uint4 u, float* v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemmKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // Dynamic shared memory: [B stages][A windows][barriers]; B stages need 1024 B alignment.
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* b_smem = base;
+  unsigned char* a_smem = b_smem + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes;
+  Smem* sm = reinterpret_cast<Smem*>(a_smem + 2 * static_cast<size_t>(pl.a_win_bytes));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = d.error_flag;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbarInit(&sm->a_full[i], 1);
+      mbarInit(&sm->a_empty[i], 1);
+      mbarInit(&sm->acc_full[i], 1);
+      mbarInit(&sm->acc_empty[i], 4);
+    }
+    for (int i = 0; i < pl.b_stages; ++i) {
+      mbarInit(&sm->b_full[i], 1);
+      mbarInit(&sm->b_empty[i], 1);
+    }
+    mbarInit(&sm->drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smemU32(&sm->tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  tcFenceAfter();
+  const uint32_t tmem = sm->tmem_base;
+  const int n_tiles_total = pl.m_tiles * pl.n_tiles;
+  const int taps_cw = d.taps * pl.cw;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer ----------------
+      const unsigned char* a_bytes = static_cast<const unsigned char*>(d.a);
+      uint32_t a_iter = 0, b_iter = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+        const int m0 = (tile / pl.n_tiles) * kBlockM;
+        const int n0 = (tile % pl.n_tiles) * BN;
+        for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
+          const int slot = a_iter & 1;
+          ok = waitBar(&sm->a_empty[slot], ((a_iter >> 1) & 1) ^ 1, err, 11);
+          if (!ok) break;
+          mbarExpectTx(&sm->a_full[slot], pl.a_win_bytes);
+          unsigned char* win = a_smem + static_cast<size_t>(slot) * pl.a_win_bytes;
+          const uint32_t plane_bytes = static_cast<uint32_t>(pl.win_rows) * 16u;
+          for (int p = 0; p < pl.planes; ++p) {
+            const unsigned char* src = a_bytes +
+                                       static_cast<long long>(ch * pl.planes + p) * d.a_plane_stride +
+                                       static_cast<long long>(m0 + pl.min_off) * 16;
+            bulkCopy(win + p * plane_bytes, src, plane_bytes, &sm->a_full[slot]);
+          }
+          ++a_iter;
+          for (int st = 0; st < pl.stages_per_chunk; ++st) {
+            const int bs = b_iter % pl.b_stages;
+            ok = waitBar(&sm->b_empty[bs], ((b_iter / pl.b_stages) & 1) ^ 1, err, 12);
+            if (!ok) break;
+            mbarExpectTx(&sm->b_full[bs], pl.b_stage_bytes);
+            tmaLoad2d(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
+                      ch * taps_cw + st * kBlockK, n0, &sm->b_full[bs]);
+            ++b_iter;
+          }
+        }
+      }
+      // Drain: every load armed above must land before the CTA may exit.
+      for (uint32_t i = a_iter > 2 ? a_iter - 2 : 0; i < a_iter; ++i) {
+        drainBar(&sm->a_full[i & 1], (i >> 1) & 1);
+      }
+      const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
+      for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
+        drainBar(&sm->b_full[i % nb], (i / nb) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = instrDesc(BN, sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value);
+      uint32_t a_iter = 0, b_iter = 0, t_iter = 0;
+      bool ok = true;
+      const uint32_t a_plane_bytes = static_cast<uint32_t>(pl.win_rows) * 16u;
+      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++t_iter) {
+        const int buf = t_iter & 1;
+        ok = waitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 13);
+        if (!ok) break;
+        tcFenceAfter();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
+        for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
+          const int slot = a_iter & 1;
+          ok = waitBar(&sm->a_full[slot], (a_iter >> 1) & 1, err, 14);
+          if (!ok) break;
+          tcFenceAfter();
+          const uint32_t win = smemU32(a_smem + static_cast<size_t>(slot) * pl.a_win_bytes);
+          for (int st = 0; st < pl.stages_per_chunk; ++st) {
+            const int bs = b_iter % pl.b_stages;
+            ok = waitBar(&sm->b_full[bs], (b_iter / pl.b_stages) & 1, err, 15);
+            if (!ok) break;
+            tcFenceAfter();
+            const uint32_t bst = smemU32(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes);
+#pragma unroll
+            for (int ks = 0; ks < kBlockK / 16; ++ks) {
+              const int k_local = st * kBlockK + ks * 16;
+              const int tap = k_local / pl.cw;
+              const int c = k_local - tap * pl.cw;
+              const uint32_t a_addr = win + static_cast<uint32_t>(d.tap_off[tap] - pl.min_off) * 16u +
+                                      static_cast<uint32_t>(c >> 3) * a_plane_bytes;
+              const uint64_t a_desc = smemDesc(a_addr, a_plane_bytes, 128u, kLayoutNone);
+              const uint64_t b_desc = smemDesc(bst + ks * 32u, 16u, 1024u, kLayoutSw128);
+              tcMma(d_tmem, a_desc, b_desc, idesc, (ch | st | ks) != 0 ? 1u : 0u);
+            }
+            tcCommit(&sm->b_empty[bs]);
+            ++b_iter;
+          }
+          tcCommit(&sm->a_empty[slot]);
+          ++a_iter;
+        }
+        tcCommit(&sm->acc_full[buf]);
+      }
+      // Drain: wait until every MMA issued above has completed.
+      tcCommit(&sm->drain);
+      waitBar(&sm->drain, 0, err, 16);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const unsigned char* res = static_cast<const unsigned char*>(d.residual);
+    unsigned char* dst = static_cast<unsigned char*>(d.dst);
+    uint32_t t_iter = 0;
+    for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t_iter) {
+      const int m0 = (tile / pl.n_tiles) * kBlockM;
+      const int n0 = (tile % pl.n_tiles) * BN;
+      const int buf = t_iter & 1;
+      if (!waitBar(&sm->acc_full[buf], (t_iter >> 1) & 1, err, 17)) break;
+      tcFenceAfter();
+      const int r = m0 + row_in_tile;
+      bool valid = r < d.rows;
+      long long drow = 0;
+      int ch_base = 0;
+      int pos_row = 0;
+      if (valid) {
+        const int img = r / d.img_rows;
+        const int loc = r - img * d.img_rows;
+        const int gy = loc / d.grid_w;
+        const int gx = loc - gy * d.grid_w;
+        valid = gy < d.valid_h && gx < d.valid_w;
+        switch (d.dst_mode) {
+          case FPK_DST_S2D:
+            drow = static_cast<long long>(img) * d.dst_img_rows + ((gy + 1) >> 1) * d.dst_grid_w +
+                   ((gx + 1) >> 1);
+            ch_base = (((gy + 1) & 1) * 2 + ((gx + 1) & 1)) * d.cout;
+            break;
+          case FPK_DST_CONCAT:
+            drow = static_cast<long long>(img % d.img_mod) * d.img_rows + loc;
+            ch_base = (img / d.img_mod) * d.ch_step;
+            break;
+          case FPK_DST_TOKENS:
+            drow = static_cast<long long>(img) * d.valid_h * d.valid_w + gy * d.valid_w + gx;
+            pos_row = gy * d.valid_w + gx;
+            break;
+          default:
+            drow = r;
+        }
+      }
+      const uint32_t t_base =
+          tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+#pragma unroll 1
+      for (int j = 0; j < BN; j += 32) {
+        uint32_t acc[32];
+        FPB_TMEM_LD32(t_base + j, acc);
+        tmemWaitLd();
+        if (valid) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int n = n0 + j + g * 8;
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[g * 8 + e]);
+            if (d.bias != nullptr) {
+              const float4 b0 = __ldg(reinterpret_cast<const float4*>(d.bias + n));
+              const float4 b1 = __ldg(reinterpret_cast<const float4*>(d.bias + n + 4));
+              v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+              v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+            }
+            if (res != nullptr) {
+              float rv[8];
+              unpack8<T>(*reinterpret_cast<const uint4*>(res + static_cast<long long>(n >> 3) *
+                                                                   d.res_plane_stride +
+                                                               static_cast<long long>(r) * 16),
+                         rv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] += rv[e];
+            }
+            if (d.relu) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = fmaxf(v[e], 0.0f);
+            }
+            if (d.dst_mode == FPK_DST_TOKENS && d.pos != nullptr) {
+              const float* pp = d.pos + static_cast<long long>(pos_row) * d.cout + n;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
+            }
+            const int cd = ch_base + n;
+            *reinterpret_cast<uint4*>(dst + static_cast<long long>(cd >> 3) * d.dst_plane_stride +
+                                      drow * 16) = pack8<T>(v);
+          }
+        }
+      }
+      tcFenceBefore();
+      __syncwarp();
+      if (lane == 0) mbarArrive(&sm->acc_empty[buf]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tcFenceAfter();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps, planning, launch.
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encodeFn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map) {
+  EncodeTiledFn enc = encodeFn();
+  if (enc == nullptr) return fail("fpk_gemm: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kprime), static_cast<cuuint64_t>(d.cout)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kprime) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(bn)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map,
+                         d.dtype == FPK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(d.w), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail("fpk_gemm: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return 0;
+}
+
+int numSms() {
+  static int value = 0;
+  if (value == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&value, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return value;
+}
+
+template <typename T, int BN>
+int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, size_t smem,
+           cudaStream_t stream) {
+  static int attr_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 31 && !(attr_mask & (1 << dev))) {
+    const cudaError_t e = cudaFuncSetAttribute(gemmKernel<T, BN>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(220 * 1024));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(std::string("fpk_gemm smem attribute: ") + cudaGetErrorString(e));
+    }
+    attr_mask |= 1 << dev;
+  }
+  const int tiles = pl.m_tiles * pl.n_tiles;
+  const int grid = tiles < numSms() ? tiles : numSms();
+  gemmKernel<T, BN><<<grid, kThreads, smem, stream>>>(d, pl, map);
+  return checkLaunch("gemmKernel");
+}
+
+}  // namespace gemm
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
+  using namespace fpb::gemm;
+  if (desc == nullptr || desc->a == nullptr || desc->w == nullptr || desc->dst == nullptr ||
+      desc->error_flag == nullptr) {
+    return fail("fpk_gemm: null pointer in descriptor");
+  }
+  const fpk_gemm_desc_t& d = *desc;
+  if (d.dtype != FPK_DTYPE_F16 && d.dtype != FPK_DTYPE_BF16) return fail("fpk_gemm: dtype must be f16 or bf16");
+  if (d.taps < 1 || d.taps > FPK_GEMM_MAX_TAPS) return fail("fpk_gemm: taps out of range");
+  if (d.cin < 32 || (d.cin != 32 && d.cin % 64 != 0)) return fail("fpk_gemm: cin must be 32 or a multiple of 64");
+  if (d.rows <= 0 || d.img_rows <= 0 || d.grid_w <= 0) return fail("fpk_gemm: bad grid");
+  if (reinterpret_cast<uintptr_t>(d.a) % 16 || d.a_plane_stride % 16 ||
+      reinterpret_cast<uintptr_t>(d.dst) % 16 || d.dst_plane_stride % 16 ||
+      reinterpret_cast<uintptr_t>(d.w) % 16 || (d.bias && reinterpret_cast<uintptr_t>(d.bias) % 16)) {
+    return fail("fpk_gemm: pointers and plane strides must be 16-byte aligned");
+  }
+  Plan pl{};
+  pl.cw = d.cin < 64 ? d.cin : 64;
+  pl.planes = pl.cw / 8;
+  pl.n_chunks = d.cin / pl.cw;
+  if ((d.taps * pl.cw) % kBlockK != 0) return fail("fpk_gemm: taps*chunk must be a multiple of 64");
+  pl.stages_per_chunk = d.taps * pl.cw / kBlockK;
+  int mn = d.tap_off[0], mx = d.tap_off[0];
+  for (int t = 1; t < d.taps; ++t) {
+    mn = d.tap_off[t] < mn ? d.tap_off[t] : mn;
+    mx = d.tap_off[t] > mx ? d.tap_off[t] : mx;
+  }
+  pl.min_off = mn;
+  pl.win_rows = kBlockM + (mx - mn);
+  pl.a_win_bytes = static_cast<uint32_t>(pl.planes * pl.win_rows * 16);
+  int bn = d.cout >= 256 ? 256 : d.cout;
+  if (d.cout % bn != 0 || (bn != 64 && bn != 128 && bn != 256)) {
+    return fail("fpk_gemm: cout must be 64, 128 or a multiple of 256");
+  }
+  pl.b_stage_bytes = static_cast<uint32_t>(bn) * 128u;
+  const size_t budget = 220 * 1024 - 1024 - sizeof(Smem) - 2 * static_cast<size_t>(pl.a_win_bytes);
+  int stages = static_cast<int>(budget / pl.b_stage_bytes);
+  if (stages > 8) stages = 8;
+  if (stages < 2) return fail("fpk_gemm: activation window too large for shared memory");
+  pl.b_stages = stages;
+  pl.m_tiles = (d.rows + kBlockM - 1) / kBlockM;
+  pl.n_tiles = d.cout / bn;
+  const size_t smem = 1024 + static_cast<size_t>(stages) * pl.b_stage_bytes +
+                      2 * static_cast<size_t>(pl.a_win_bytes) + sizeof(Smem);
+  const int kprime = pl.n_chunks * d.taps * pl.cw;
+  CUtensorMap map;
+  if (makeWeightMap(d, kprime, bn, &map) != 0) return 1;
+  auto s = static_cast<cudaStream_t>(stream);
+  const bool bf = d.dtype == FPK_DTYPE_BF16;
+  switch (bn) {
+    case 64:
+      return bf ? launch<__nv_bfloat16, 64>(d, pl, map, smem, s) : launch<__half, 64>(d, pl, map, smem, s);
+    case 128:
+      return bf ? launch<__nv_bfloat16, 128>(d, pl, map, smem, s) : launch<__half, 128>(d, pl, map, smem, s);
+    default:
+      return bf ? launch<__nv_bfloat16, 256>(d, pl, map, smem, s) : launch<__half, 256>(d, pl, map, smem, s);
+  }
+}

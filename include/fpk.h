@@ -1,0 +1,191 @@
+/*
+ * fpk: kernel-level C ABI of the FoundationPose B200 runtime.
+ *
+ * These are the sm_100a kernels behind libfoundation_pose_nvidia.so, exported
+ * with plain pointers and sizes (no C++ or torch types) so tests, benchmarks
+ * and FFI callers can drive each hot-path stage on their own device buffers.
+ * All array pointers are DEVICE pointers unless marked (host). `stream` is a
+ * cudaStream_t (NULL = legacy default stream). Every call is asynchronous on
+ * `stream`; it returns 0 on success or a non-zero code and records a message
+ * readable through fpk_last_error() (thread-local).
+ *
+ * Each entry point names the reference interface it replaces
+ * (paths inside nvidia-isaac/foundation-pose-inference-library).
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "foundation_pose_nvidia/c_api.h" /* FP_API */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Hot-path fields of the reference Config (include/foundation_pose_nvidia/config.hpp:20-67). */
+typedef struct fpk_params {
+  float depth_min, depth_max;
+  int erosion_radius, bilateral_radius;
+  float depth_diff_threshold, erosion_ratio_threshold, bilateral_sigma_d, bilateral_sigma_r;
+  float crop_ratio;
+  int input_width, input_height;
+  float rotation_normalizer_rad, znear, zfar, ambient_weight, diffuse_weight;
+} fpk_params_t;
+
+/* Camera intrinsics fx, fy, cx, cy (reference types.hpp:174-192). */
+typedef struct fpk_intrinsics {
+  float fx, fy, cx, cy;
+} fpk_intrinsics_t;
+
+/* Device mesh in the centred object frame (reference cuda_pipeline.hpp:21-35).
+ * colors are float RGB in [0,1]; uvs/texture optional (NULL / 0). */
+typedef struct fpk_mesh {
+  const float* vertices;  /* [n_vertices*3] */
+  const float* normals;   /* [n_vertices*3] */
+  const float* colors;    /* [n_vertices*3] */
+  const float* uvs;       /* [n_vertices*2] or NULL */
+  const float* texture;   /* [texture_height*texture_width*3] or NULL */
+  const int32_t* faces;   /* [n_faces*3] */
+  int n_vertices;
+  int n_faces;
+  int texture_width;
+  int texture_height;
+} fpk_mesh_t;
+
+/* Network-input element types for fpk_render_pack. */
+#define FPK_DTYPE_F32 0
+#define FPK_DTYPE_F16 1
+#define FPK_DTYPE_BF16 2
+
+/* Size in int32 of the translation-statistics scratch (bbox, count, 65,536-bin histogram). */
+#define FPK_STATS_INTS (8 + 65536)
+
+FP_API const char* fpk_last_error(void);
+FP_API void fpk_default_params(fpk_params_t* p);
+
+/* Fused depth erode -> bilateral -> (xyz) -> mask statistics, one pass over the frame.
+ * Replaces runDepthPreprocess + runDepthToXyz + the statistics half of
+ * runInitialTranslation (reference src/cuda_pipeline.cu:743-796).
+ * mask may be NULL (track: no statistics). stats must hold FPK_STATS_INTS
+ * int32 and is zeroed by this call when mask != NULL. eroded and xyz are
+ * optional outputs (NULL to skip). */
+FP_API int fpk_preprocess(const float* depth_raw, const uint8_t* mask, int width, int height,
+                          fpk_intrinsics_t k, const fpk_params_t* p, float* depth_filtered,
+                          float* eroded, float* xyz, int32_t* stats, void* stream);
+
+/* Median-depth translation + pose seeding. Replaces finalizeTranslationKernel +
+ * seedPosesKernel (reference src/cuda_pipeline.cu:239-278, 301-327, 797-812).
+ * rotations [n*9] row-major; writes t0 [3] and poses [n*16]; re-zeroes nothing. */
+FP_API int fpk_seed_poses(const int32_t* stats, const float* rotations, int n, fpk_intrinsics_t k,
+                          const fpk_params_t* p, float* t0, float* poses, void* stream);
+
+/* Square crop boxes (l, t, r, b) per pose. Replaces computeCropBoxesOnDevice
+ * (reference src/cuda_pipeline.cu:814-826). */
+FP_API int fpk_crop_boxes(const float* poses, int n, fpk_intrinsics_t k, float diameter,
+                          const fpk_params_t* p, float* boxes, void* stream);
+
+/* Rasterize + shade every hypothesis into its crop: NHWC float3 RGB and camera
+ * XYZ, rows top-down. Replaces IRenderer::render / BuiltinRasterRenderer::render
+ * (reference src/builtin_raster_renderer.cu:218-281, raster_kernels.cuh:336-495).
+ * boxes are read (compute them with fpk_crop_boxes). tri_ids (optional,
+ * [n*H*W] int32, rows bottom-up like the reference rast buffer) receives
+ * triangle_index+1, 0 = background. */
+FP_API int fpk_render(const fpk_mesh_t* mesh, const float* poses, const float* boxes, int n,
+                      fpk_intrinsics_t k, const fpk_params_t* p, float* out_rgb, float* out_xyz,
+                      int32_t* tri_ids, void* stream);
+
+/* Crop-warp + normalisation into the two NCHW [n,6,H,W] fp32 network inputs.
+ * Replaces prepareNetworkInputsOnDevice (reference src/cuda_pipeline.cu:434-511, 828-845).
+ * Observed XYZ is back-projected from depth_filtered on the fly. */
+FP_API int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, int height,
+                    fpk_intrinsics_t k, const fpk_params_t* p, const float* rend_rgb,
+                    const float* rend_xyz, const float* poses, const float* boxes, int n,
+                    float diameter, float invalid_depth_threshold, float* net_rendered,
+                    float* net_observed, void* stream);
+
+/* Fused crop boxes + rasterize + shade + crop-warp + pack: one CTA per
+ * (hypothesis, row band), z-buffer resident in shared memory, writing both
+ * network inputs straight into the stem's space-to-depth KP8 layout: crop pixel
+ * (y, x) of image i (rendered i = 0..n-1, observed n+i) goes to plane
+ * ((y+3)%2)*2 + (x+3)%2, row i*gh*gw + ((y+3)/2)*gw + (x+3)/2 with
+ * gh = (H+7)/2, gw = (W+7)/2 (83 x 83 for 160 x 160 crops): 16 bytes = 6 values
+ * + 2 zeros of `dtype`. net_input points at row 0 of plane 0; planes are
+ * plane_stride bytes apart. Rows never written (the zero border of the grid)
+ * must be zero before first use. Replaces the computeCropBoxes ->
+ * IRenderer::render -> prepareNetworkInputs sequence (reference
+ * src/foundation_pose.cpp:429-443). boxes (optional) receives the crop boxes. */
+FP_API int fpk_render_pack(const fpk_mesh_t* mesh, const float* poses, int n,
+                           const uint8_t* rgb, const float* depth_filtered, int width, int height,
+                           fpk_intrinsics_t k, const fpk_params_t* p, float diameter,
+                           float invalid_depth_threshold, int dtype, void* net_input,
+                           long long plane_stride, float* boxes, void* stream);
+
+/* R <- exp(tanh(dr)*norm)^T R; t += dt*diameter/2. Replaces applyPoseDeltasOnDevice
+ * (reference src/cuda_pipeline.cu:513-547, 847-858). In place. */
+FP_API int fpk_apply_deltas(float* poses, const float* delta_t, const float* delta_r, int n,
+                            float diameter, const fpk_params_t* p, void* stream);
+
+/* Arg-max of scores (first maximum wins) + un-centre by the mesh centre (host
+ * center3). result = {pose[16], score, index-as-int32}. Replaces
+ * selectBestPoseOnDevice (reference src/cuda_pipeline.cu:549-582, 860-868). */
+FP_API int fpk_select_best(const float* poses, const float* scores, int n, const float* center3,
+                           float* result, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-core GEMM / implicit convolution (tcgen05 + TMEM, sm_100a).
+ *
+ * Activations use the channel-group planar layout ("KP8"): plane p holds
+ * channels 8p..8p+7 of every row as one 16-byte record, so row r of plane p
+ * is at base + p*plane_stride + r*16 bytes. Every plane carries zeroed guard
+ * rows before row 0 and after the last row, so shifted convolution windows
+ * may start at negative rows.
+ *
+ * out[r, n] = epilogue( sum_t sum_c A[r + tap_off[t], c] * W[n, t, c] + bias[n] )
+ * over rows r of a padded spatial grid (img_rows = grid rows per image,
+ * grid_w = grid width; rows whose (gy, gx) falls outside valid_h x valid_w are
+ * computed but not stored). W is [cout][K'] with K' = (cin/cw)*taps*cw in
+ * chunk-major order: k' = chunk*(taps*cw) + tap*cw + c, cw = min(cin, 64).
+ * dst_mode selects where row r / channel n lands:
+ *   SAME   (r, n)
+ *   S2D    space-to-depth for a following stride-2 conv: cell ((gy+1)/2, (gx+1)/2)
+ *          of a dst grid (dst_img_rows, dst_grid_w), channel ((gy+1)%2*2+(gx+1)%2)*cout + n
+ *   CONCAT image i -> image i % img_mod, channel (i / img_mod)*ch_step + n
+ *   TOKENS dense rows img*valid_h*valid_w + gy*valid_w + gx, adding pos[(gy*valid_w+gx)*cout + n]
+ * Replaces the TensorRT engines' convolution / matmul layers behind
+ * IInferenceRunner::enqueueRefine / enqueueScore (reference
+ * src/tensorrt_runner.cu:367-407). */
+#define FPK_DST_SAME 0
+#define FPK_DST_S2D 1
+#define FPK_DST_CONCAT 2
+#define FPK_DST_TOKENS 3
+#define FPK_GEMM_MAX_TAPS 16
+
+typedef struct fpk_gemm_desc {
+  const void* a;
+  long long a_plane_stride;
+  int rows;
+  int cin;
+  int taps;
+  int tap_off[FPK_GEMM_MAX_TAPS];
+  const void* w;
+  int cout;
+  const float* bias;
+  const void* residual; /* same layout/grid as A (KP8, cout channels), or NULL */
+  long long res_plane_stride;
+  int relu;
+  void* dst;
+  long long dst_plane_stride;
+  int dst_mode;
+  int img_rows, grid_w, valid_h, valid_w;
+  int dst_img_rows, dst_grid_w, img_mod, ch_step;
+  const float* pos;
+  int dtype;       /* FPK_DTYPE_F16 or FPK_DTYPE_BF16 */
+  int* error_flag; /* device int32; set non-zero if a pipeline wait times out */
+} fpk_gemm_desc_t;
+
+FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif

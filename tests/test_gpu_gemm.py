@@ -1,0 +1,236 @@
+"""GPU tests of the tcgen05 implicit-GEMM kernel (fpk_gemm) against torch fp32
+on the same half-precision-rounded operands. Tolerance: 1e-2 of the output's
+max magnitude (fp16/bf16 output rounding; fp32 accumulation)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.nn.functional as F  # noqa: E402
+
+from fp_b200.kernels import (FPK_DST_S2D, FPK_DST_SAME, FPK_DST_TOKENS, FPK_DTYPE_BF16,  # noqa: E402
+                             FPK_DTYPE_F16, GemmDesc, gemm)
+from kp8_util import Planar  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16}
+
+
+def make_desc(a: Planar, rows, cin, taps_off, w, cout, dst: Planar, dtype, err, bias=None,
+              residual: Planar | None = None, relu=False, mode=FPK_DST_SAME, img_rows=None,
+              grid_w=1, valid_h=None, valid_w=1, dst_img_rows=0, dst_grid_w=0, pos=None):
+    d = GemmDesc()
+    d.a, d.a_plane_stride, d.rows, d.cin = a.base, a.plane_stride, rows, cin
+    d.taps = len(taps_off)
+    for i, o in enumerate(taps_off):
+        d.tap_off[i] = int(o)
+    d.w, d.cout = w.data_ptr(), cout
+    d.bias = bias.data_ptr() if bias is not None else None
+    d.residual = residual.base if residual is not None else None
+    d.res_plane_stride = residual.plane_stride if residual is not None else 0
+    d.relu = int(relu)
+    d.dst, d.dst_plane_stride, d.dst_mode = dst.base, dst.plane_stride, mode
+    d.img_rows = img_rows or rows
+    d.grid_w, d.valid_h, d.valid_w = grid_w, valid_h or (img_rows or rows), valid_w
+    d.dst_img_rows, d.dst_grid_w, d.img_mod, d.ch_step = dst_img_rows, dst_grid_w, 1, 0
+    d.pos = pos.data_ptr() if pos is not None else None
+    d.dtype = dtype
+    d.error_flag = err.data_ptr()
+    return d
+
+
+def chunk_major(w_taps: torch.Tensor) -> torch.Tensor:
+    """[cout, taps, cin] -> [cout, K'] with k' = chunk*(taps*cw) + tap*cw + c."""
+    cout, taps, cin = w_taps.shape
+    cw = min(cin, 64)
+    return (w_taps.reshape(cout, taps, cin // cw, cw).permute(0, 2, 1, 3)
+            .reshape(cout, taps * cin).contiguous())
+
+
+def close(got: torch.Tensor, want: torch.Tensor, tol=1e-2):
+    scale = want.abs().max().item() + 1e-6
+    err = (got.float() - want.float()).abs().max().item()
+    assert err <= tol * scale, f"max err {err:.3e} vs scale {scale:.3e}"
+
+
+@pytest.fixture()
+def err():
+    return torch.zeros(1, dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("m,cin,cout,dtype", [(1000, 64, 64, FPK_DTYPE_BF16),
+                                              (777, 128, 128, FPK_DTYPE_F16),
+                                              (2000, 256, 256, FPK_DTYPE_BF16),
+                                              (513, 512, 512, FPK_DTYPE_BF16),
+                                              (4096, 512, 1536, FPK_DTYPE_F16)])
+def test_plain_gemm(fpk, err, m, cin, cout, dtype):
+    g = torch.Generator().manual_seed(m + cin)
+    dt = DT[dtype]
+    A = torch.randn(m, cin, generator=g)
+    W = torch.randn(cout, cin, generator=g) / math.sqrt(cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+    pa = Planar(m, cin, dt).set(A.to(DEV))
+    out = Planar(m, cout, dt)
+    w = chunk_major(W.reshape(cout, 1, cin)).to(dt).to(DEV)
+    gemm(fpk, make_desc(pa, m, cin, [0], w, cout, out, dtype, err, bias=b))
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ref = A.to(dt).float().to(DEV) @ W.to(dt).float().to(DEV).T + b
+    close(out.get(), ref)
+    # Rows outside [0, m) of the destination (guard rows) were not touched.
+    assert torch.count_nonzero(out.t[:, :256]) == 0
+
+
+@pytest.mark.parametrize("cin,cout,hw,dtype", [(64, 128, 20, FPK_DTYPE_BF16),
+                                               (128, 128, 40, FPK_DTYPE_F16),
+                                               (256, 256, 40, FPK_DTYPE_BF16),
+                                               (512, 512, 20, FPK_DTYPE_BF16)])
+def test_conv3x3_residual_relu(fpk, err, cin, cout, hw, dtype):
+    g = torch.Generator().manual_seed(cin * 7 + hw)
+    dt = DT[dtype]
+    n, H, W = 3, hw, hw
+    gw = W + 1
+    img_rows = (H + 1) * gw
+    rows = n * img_rows
+    X = torch.randn(n, cin, H, W, generator=g)
+    R = torch.randn(n, cout, H, W, generator=g)
+    Wt = torch.randn(cout, cin, 3, 3, generator=g) / math.sqrt(9 * cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+
+    def to_grid(t):  # [n,C,H,W] -> [rows, C] on the (H+1)x(W+1) grid, zero border row/col
+        c = t.shape[1]
+        z = torch.zeros(n, H + 1, W + 1, c)
+        z[:, :H, :W] = t.permute(0, 2, 3, 1)
+        return z.reshape(rows, c)
+
+    pa = Planar(rows, cin, dt).set(to_grid(X).to(DEV))
+    pr = Planar(rows, cout, dt).set(to_grid(R).to(DEV))
+    out = Planar(rows, cout, dt)
+    taps = [(ky - 1) * gw + (kx - 1) for ky in range(3) for kx in range(3)]
+    w = chunk_major(Wt.permute(0, 2, 3, 1).reshape(cout, 9, cin)).to(dt).to(DEV)
+    gemm(fpk, make_desc(pa, rows, cin, taps, w, cout, out, dtype, err, bias=b, residual=pr,
+                        relu=True, img_rows=img_rows, grid_w=gw, valid_h=H, valid_w=W))
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ref = F.conv2d(X.to(dt).float().to(DEV), Wt.to(dt).float().to(DEV), b, padding=1)
+    ref = torch.relu(ref + R.to(dt).float().to(DEV))
+    got = out.get().reshape(n, H + 1, W + 1, cout)
+    close(got[:, :H, :W], ref.permute(0, 2, 3, 1))
+    # The zero border row/column of the output grid stays zero.
+    assert torch.count_nonzero(got[:, H]) == 0 and torch.count_nonzero(got[:, :, W]) == 0
+
+
+def s2d_weights(Wt: torch.Tensor, stride_taps: int, sub_offset: int) -> torch.Tensor:
+    """Stride-2 conv weights [cout, cin, k, k] -> taps over space-to-depth input:
+    tap (a, b) in stride_taps^2, channel (sub=(dy,dx), c) with k index 2a+dy."""
+    cout, cin, k, _ = Wt.shape
+    out = torch.zeros(cout, stride_taps * stride_taps, 4 * cin)
+    for a in range(stride_taps):
+        for bb in range(stride_taps):
+            for dy in range(2):
+                for dx in range(2):
+                    ky, kx = 2 * a + dy, 2 * bb + dx
+                    if ky < k and kx < k:
+                        sub = dy * 2 + dx
+                        out[:, a * stride_taps + bb, sub * cin:(sub + 1) * cin] = Wt[:, :, ky, kx]
+    return out
+
+
+@pytest.mark.parametrize("dtype", [FPK_DTYPE_BF16, FPK_DTYPE_F16])
+def test_s2d_stride2_conv(fpk, err, dtype):
+    """1x1 layer writing space-to-depth, then a 3x3 stride-2 conv as a 2x2 conv."""
+    g = torch.Generator().manual_seed(5)
+    dt = DT[dtype]
+    n, H2, c1, c2 = 2, 40, 64, 128
+    H = H2 // 2
+    gw1 = H2 + 1
+    rows1 = n * (H2 + 1) * gw1
+    X = torch.randn(n, c1, H2, H2, generator=g)
+    W1 = torch.randn(c1, c1, generator=g) / math.sqrt(c1)
+    W2 = torch.randn(c2, c1, 3, 3, generator=g) / math.sqrt(9 * c1)
+    b1 = torch.zeros(c1).to(DEV)
+    b2 = torch.randn(c2, generator=g).to(DEV)
+    z = torch.zeros(n, H2 + 1, H2 + 1, c1)
+    z[:, :H2, :H2] = X.permute(0, 2, 3, 1)
+    pa = Planar(rows1, c1, dt).set(z.reshape(rows1, c1).to(DEV))
+    gw2 = H + 1
+    rows2 = n * (H + 1) * gw2
+    t2 = Planar(rows2, 4 * c1, dt)
+    w1 = chunk_major(W1.reshape(c1, 1, c1)).to(dt).to(DEV)
+    gemm(fpk, make_desc(pa, rows1, c1, [0], w1, c1, t2, dtype, err, bias=b1, relu=False,
+                        mode=FPK_DST_S2D, img_rows=(H2 + 1) * gw1, grid_w=gw1, valid_h=H2,
+                        valid_w=H2, dst_img_rows=(H + 1) * gw2, dst_grid_w=gw2))
+    out = Planar(rows2, c2, dt)
+    taps = [a * gw2 + bb for a in range(2) for bb in range(2)]
+    w2 = chunk_major(s2d_weights(W2, 2, 1)).to(dt).to(DEV)
+    gemm(fpk, make_desc(t2, rows2, 4 * c1, taps, w2, c2, out, dtype, err, bias=b2, relu=True,
+                        img_rows=(H + 1) * gw2, grid_w=gw2, valid_h=H, valid_w=H))
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    y = torch.einsum("nchw,dc->ndhw", X.to(dt).float(), W1.to(dt).float()).to(dt).float()
+    ref = torch.relu(F.conv2d(y.to(DEV), W2.to(dt).float().to(DEV), b2, stride=2, padding=1))
+    got = out.get().reshape(n, H + 1, gw2, c2)[:, :H, :H]
+    close(got, ref.permute(0, 2, 3, 1))
+
+
+@pytest.mark.parametrize("dtype", [FPK_DTYPE_BF16])
+def test_stem_7x7_stride2(fpk, err, dtype):
+    """7x7 stride-2 pad-3 conv over 6 channels as a 16-tap conv on the 32-channel
+    space-to-depth layout the fused render+pack writes (grid 83 for 160 crops)."""
+    g = torch.Generator().manual_seed(9)
+    dt = DT[dtype]
+    n, S, cin, cout = 2, 160, 6, 64
+    gs = (S + 7) // 2  # 83
+    X = torch.randn(n, cin, S, S, generator=g)
+    Wt = torch.randn(cout, cin, 7, 7, generator=g) / math.sqrt(49 * cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+    # Space-to-depth input: cell (gy, gx), sub (dy, dx) holds in[2gy+dy-3, 2gx+dx-3].
+    T = torch.zeros(n, gs, gs, 4, 8)
+    xp = torch.zeros(n, cin, 2 * gs, 2 * gs)
+    xp[:, :, 3:3 + S, 3:3 + S] = X
+    for dy in range(2):
+        for dx in range(2):
+            T[:, :, :, dy * 2 + dx, :cin] = xp[:, :, dy::2, dx::2].permute(0, 2, 3, 1)
+    rows = n * gs * gs
+    pa = Planar(rows, 32, dt).set(T.reshape(rows, 32).to(DEV))
+    Wp = torch.zeros(cout, cin + 2, 7, 7)
+    Wp[:, :cin] = Wt
+    w = chunk_major(s2d_weights(Wp, 4, 3)).to(dt).to(DEV)
+    out = Planar(rows, cout, dt)
+    taps = [a * gs + bb for a in range(4) for bb in range(4)]
+    gemm(fpk, make_desc(pa, rows, 32, taps, w, cout, out, dtype, err, bias=b, relu=True,
+                        img_rows=gs * gs, grid_w=gs, valid_h=S // 2, valid_w=S // 2))
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ref = torch.relu(F.conv2d(X.to(dt).float().to(DEV), Wt.to(dt).float().to(DEV), b, stride=2,
+                              padding=3))
+    got = out.get().reshape(n, gs, gs, cout)[:, :S // 2, :S // 2]
+    close(got, ref.permute(0, 2, 3, 1))
+
+
+def test_tokens_epilogue(fpk, err):
+    g = torch.Generator().manual_seed(3)
+    dt = torch.bfloat16
+    n, H, cin, cout = 3, 20, 128, 256
+    gw = H + 1
+    rows = n * (H + 1) * gw
+    X = torch.randn(n, H, H, cin, generator=g)
+    z = torch.zeros(n, H + 1, gw, cin)
+    z[:, :H, :H] = X
+    Wt = torch.randn(cout, cin, generator=g) / math.sqrt(cin)
+    pos = torch.randn(H * H, cout, generator=g).to(DEV)
+    pa = Planar(rows, cin, dt).set(z.reshape(rows, cin).to(DEV))
+    out = Planar(n * H * H, cout, dt)
+    w = chunk_major(Wt.reshape(cout, 1, cin)).to(dt).to(DEV)
+    gemm(fpk, make_desc(pa, rows, cin, [0], w, cout, out, FPK_DTYPE_BF16, err, relu=True,
+                        mode=FPK_DST_TOKENS, img_rows=(H + 1) * gw, grid_w=gw, valid_h=H,
+                        valid_w=H, pos=pos))
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ref = torch.relu(X.reshape(n, H * H, cin).to(dt).float().to(DEV) @ Wt.to(dt).float().to(DEV).T)
+    ref = ref + pos[None]
+    close(out.get().reshape(n, H * H, cout), ref)
