@@ -1,0 +1,48 @@
+// Launchers of the non-GEMM network kernels (fp_net_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace fpb {
+namespace net {
+
+// Self-attention over KP8 q/k/v planes. For layer z and head h the query /
+// key / value channels are planes z*qkv_layer_planes + {q,k,v}_plane + 16h;
+// the output goes to planes z*out_layer_planes + 16h. Head dim 128.
+struct AttnArgs {
+  const unsigned char* qkv;
+  long long qkv_plane_stride;
+  int qkv_layer_planes;
+  int q_plane, k_plane, v_plane;
+  unsigned char* out;
+  long long out_plane_stride;
+  int out_layer_planes;
+  int seq_len;
+  int heads;
+  float scale_log2;  // log2(e) / sqrt(head_dim)
+};
+
+struct LnArgs {
+  const unsigned char* in;
+  long long in_plane_stride;
+  unsigned char* out;
+  long long out_plane_stride;
+  long long rows;
+  const float* gamma;
+  const float* beta;
+  float eps;
+};
+
+cudaError_t launchAttention(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s);
+cudaError_t launchLayerNorm(const LnArgs& a, bool bf16, cudaStream_t s);
+cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int seq_len, int n_seq,
+                            float* out, bool bf16, cudaStream_t s);
+cudaError_t launchLinearF32(const float* x, const float* w, const float* b, float* y, int m, int n,
+                            int k, bool relu, cudaStream_t s);
+cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStream_t s);
+cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n, int H, int W,
+                             void* dst, long long plane_stride, bool bf16, cudaStream_t s);
+cudaError_t launchConvert(const float* in, void* out, long long n, bool bf16, cudaStream_t s);
+
+}  // namespace net
+}  // namespace fpb

@@ -67,6 +67,11 @@ _SIGS = {
     "fpk_apply_deltas": (C.c_int, [_P, _P, _P, C.c_int, C.c_float, C.POINTER(Params), _P]),
     "fpk_select_best": (C.c_int, [_P, _P, C.c_int, C.POINTER(C.c_float), _P, _P]),
     "fpk_gemm": (C.c_int, [_P, _P]),
+    "fpk_net_create": (C.c_void_p, [C.c_char_p, C.c_char_p, C.c_int, C.c_int]),
+    "fpk_net_destroy": (None, [_P]),
+    "fpk_net_refine": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P]),
+    "fpk_net_score": (C.c_int, [_P, _P, _P, C.c_int, _P, _P]),
+    "fpk_net_error": (C.c_int, [_P, C.POINTER(C.c_int)]),
 }
 
 
@@ -167,3 +172,34 @@ def gemm(fl: "FpkLibrary", desc: GemmDesc, stream=0) -> None:
         _bind_gemm(fl.lib)
         fl._gemm_bound = True
     fl._check(fl.lib.fpk_gemm(C.byref(desc), stream or None), "fpk_gemm")
+
+
+class Networks:
+    """RefineNet + ScoreNet handle (fpk_net_*); precision 2 = FP16, 3 = BF16."""
+
+    def __init__(self, fl: FpkLibrary, refine_pack, score_pack, precision: int, max_batch: int):
+        self.fl = fl
+        self.h = fl.lib.fpk_net_create(str(refine_pack).encode(), str(score_pack).encode(),
+                                       int(precision), int(max_batch))
+        if not self.h:
+            raise FpkError(f"fpk_net_create: {fl.lib.fpk_last_error().decode()}")
+
+    def refine(self, rendered, observed, n, trans, rot, stream=0):
+        self.fl._check(self.fl.lib.fpk_net_refine(self.h, rendered, observed, n, trans, rot,
+                                                  stream or None), "fpk_net_refine")
+
+    def score(self, rendered, observed, n, scores, stream=0):
+        self.fl._check(self.fl.lib.fpk_net_score(self.h, rendered, observed, n, scores,
+                                                 stream or None), "fpk_net_score")
+
+    def error_flag(self) -> int:
+        v = C.c_int(0)
+        self.fl._check(self.fl.lib.fpk_net_error(self.h, C.byref(v)), "fpk_net_error")
+        return v.value
+
+    def close(self):
+        if self.h:
+            self.fl.lib.fpk_net_destroy(self.h)
+            self.h = None
+
+    __del__ = close

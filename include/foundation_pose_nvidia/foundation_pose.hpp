@@ -1,0 +1,60 @@
+// Estimator (reference include/foundation_pose_nvidia/foundation_pose.hpp:24-66):
+// register / track on one object, with injectable renderer and inference
+// backends. With the built-in backends the render, crop-warp and pack run as
+// one fused kernel writing the networks' input layout directly; injected
+// backends go through the NCHW fp32 seam exactly as in the reference.
+#pragma once
+
+#include <cstdint>
+#include <filesystem>
+#include <memory>
+#include <span>
+
+#include "foundation_pose_nvidia/config.hpp"
+#include "foundation_pose_nvidia/inference_runner.hpp"
+#include "foundation_pose_nvidia/renderer.hpp"
+#include "foundation_pose_nvidia/types.hpp"
+
+namespace foundation_pose_nvidia {
+
+Mesh loadMesh(const std::filesystem::path& path);
+void computeVertexNormals(Mesh& mesh);
+PreprocessedMesh preprocessMesh(const Mesh& mesh, const Config& config);
+
+class FoundationPose {
+ public:
+  FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_options, Config config = {});
+  FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_options,
+                 std::unique_ptr<IInferenceRunner> inference_runner,
+                 std::unique_ptr<IRenderer> renderer, Config config = {});
+  ~FoundationPose();
+  FoundationPose(const FoundationPose&) = delete;
+  FoundationPose& operator=(const FoundationPose&) = delete;
+  FoundationPose(FoundationPose&&) noexcept;
+  FoundationPose& operator=(FoundationPose&&) noexcept;
+
+  static FoundationPose createFromCadFile(const std::filesystem::path& cad_path,
+                                          RuntimeOptions runtime_options, Config config = {});
+  static FoundationPose createFromReferenceImages(std::span<const ModelFreeReferenceView> references,
+                                                  RuntimeOptions runtime_options,
+                                                  Config config = {});
+
+  void prepareForBatch(int batch_size);
+
+  PoseEstimate registerFrame(const std::uint8_t* rgb_u8, const float* depth_m,
+                             const std::uint8_t* mask_u8, int width, int height,
+                             CameraIntrinsics intrinsics, int n_refine = -1, int n_hypotheses = -1);
+
+  PoseEstimate trackFrame(const std::uint8_t* rgb_u8, const float* depth_m, int width, int height,
+                          CameraIntrinsics intrinsics, int n_refine = -1);
+
+  const PreprocessedMesh& mesh() const;
+  const Config& config() const;
+
+  struct Impl;
+
+ private:
+  std::unique_ptr<Impl> impl_;
+};
+
+}  // namespace foundation_pose_nvidia

@@ -186,6 +186,25 @@ typedef struct fpk_gemm_desc {
 
 FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * RefineNet / ScoreNet as a unit: the built-in inference backend behind
+ * IInferenceRunner (reference include/foundation_pose_nvidia/inference_runner.hpp:12-30,
+ * src/tensorrt_runner.cu:498-532). Weight packs (.fpw) replace the ONNX files;
+ * precision is FP_PRECISION_FP16 or FP_PRECISION_BF16 in this build.
+ * Inputs are NCHW [n,6,160,160] fp32 device tensors (rendered = inputA,
+ * observed = inputB); outputs are device fp32 trans/rot [n,3] and score [n].
+ * A handle owns its device memory for max_batch hypotheses on the current device. */
+typedef struct fpk_net fpk_net_t;
+FP_API fpk_net_t* fpk_net_create(const char* refine_pack, const char* score_pack, int precision,
+                                 int max_batch);
+FP_API void fpk_net_destroy(fpk_net_t* net);
+FP_API int fpk_net_refine(fpk_net_t* net, const float* rendered, const float* observed, int n,
+                          float* trans, float* rot, void* stream);
+FP_API int fpk_net_score(fpk_net_t* net, const float* rendered, const float* observed, int n,
+                         float* scores, void* stream);
+/* Device error flag of the pipelined kernels: 0 = ok (non-zero after a wait timed out). */
+FP_API int fpk_net_error(fpk_net_t* net, int* host_flag);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,98 @@
+"""GPU parity of RefineNet / ScoreNet (fpk_net_*, tcgen05 GEMMs + attention)
+against the torch fp32 reference (oracle/fp_net_ref.py) on the same weight
+pack and inputs. Bar: outputs within 1e-2 relative at FP16/BF16 (relative to
+the output's largest magnitude, per output tensor)."""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from fp_b200.kernels import Networks  # noqa: E402
+from fp_b200.weights import make_default_packs, read_pack  # noqa: E402
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "oracle"))
+from fp_net_ref import NetRef  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+FP16, BF16 = 2, 3
+
+
+@pytest.fixture(scope="module")
+def packs(tmp_path_factory):
+    return make_default_packs(tmp_path_factory.mktemp("packs"), seed=7)
+
+
+def inputs(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    rgb = torch.rand(2, n, 3, 160, 160, generator=g)
+    xyz = (torch.randn(2, n, 3, 160, 160, generator=g) * 0.5).clamp(-1.9, 1.9)
+    xyz = xyz * (torch.rand(2, n, 1, 160, 160, generator=g) > 0.3)
+    x = torch.cat([rgb, xyz], 2).float()
+    return x[0].contiguous().to(DEV), x[1].contiguous().to(DEV)
+
+
+def rel_err(got, want):
+    return ((got.float() - want.float()).abs().max() / (want.float().abs().max() + 1e-6)).item()
+
+
+@pytest.fixture(scope="module")
+def ref_models(packs):
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    return (NetRef(read_pack(packs[0])[1], device=DEV), NetRef(read_pack(packs[1])[1], device=DEV))
+
+
+@pytest.mark.parametrize("precision", [FP16, BF16])
+def test_refine_matches_reference(fpk, packs, ref_models, precision):
+    n = 3
+    A, B = inputs(n, 1)
+    net = Networks(fpk, packs[0], packs[1], precision, max_batch=8)
+    trans = torch.zeros(n, 3, device=DEV)
+    rot = torch.zeros(n, 3, device=DEV)
+    net.refine(A.data_ptr(), B.data_ptr(), n, trans.data_ptr(), rot.data_ptr())
+    torch.cuda.synchronize()
+    assert net.error_flag() == 0
+    rt, rr = ref_models[0].refine(A, B)
+    e_t, e_r = rel_err(trans, rt), rel_err(rot, rr)
+    print(f"refine precision={precision} rel err trans {e_t:.2e} rot {e_r:.2e}")
+    assert e_t <= 1e-2 and e_r <= 1e-2
+    net.close()
+
+
+@pytest.mark.parametrize("precision", [FP16, BF16])
+def test_score_matches_reference(fpk, packs, ref_models, precision):
+    n = 6
+    A, B = inputs(n, 2)
+    net = Networks(fpk, packs[0], packs[1], precision, max_batch=8)
+    scores = torch.zeros(n, device=DEV)
+    net.score(A.data_ptr(), B.data_ptr(), n, scores.data_ptr())
+    torch.cuda.synchronize()
+    assert net.error_flag() == 0
+    rs = ref_models[1].score(A, B)
+    e = rel_err(scores, rs)
+    print(f"score precision={precision} rel err {e:.2e} argmax {scores.argmax().item()} vs {rs.argmax().item()}")
+    assert e <= 1e-2
+    net.close()
+
+
+def test_refine_batch_independence(fpk, packs):
+    """RefineNet is per-hypothesis: a hypothesis gives the same output alone and
+    inside a batch (deterministic kernels, no cross-sample reductions)."""
+    A, B = inputs(4, 3)
+    net = Networks(fpk, packs[0], packs[1], FP16, max_batch=8)
+    t4 = torch.zeros(4, 3, device=DEV)
+    r4 = torch.zeros(4, 3, device=DEV)
+    net.refine(A.data_ptr(), B.data_ptr(), 4, t4.data_ptr(), r4.data_ptr())
+    t1 = torch.zeros(1, 3, device=DEV)
+    r1 = torch.zeros(1, 3, device=DEV)
+    A2, B2 = A[2:3].contiguous(), B[2:3].contiguous()
+    net.refine(A2.data_ptr(), B2.data_ptr(), 1, t1.data_ptr(), r1.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(t4[2], t1[0]) and torch.equal(r4[2], r1[0])
+    net.close()
