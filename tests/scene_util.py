@@ -80,3 +80,18 @@ def hypotheses(oracle, scene: Scene, n: int, seed: int = 0, jitter_t: float = 0.
     idx = rng.choice(rots.shape[0], size=n, replace=False)
     t = scene.gt_pose[:3, 3] + rng.normal(0, jitter_t, size=3).astype(np.float32)
     return oracle.seed_poses(rots[idx], t.astype(np.float32))
+
+
+def write_obj(path, verts, faces, colors_u8) -> None:
+    """OBJ with per-vertex colours in [0, 1] written as (c + 0.5) / 255 (255 as
+    1.0) so the loader's scale-by-255-and-truncate recovers c exactly;
+    vertices round-trip in %.9g."""
+    def enc(c):
+        return 1.0 if c >= 255 else (float(c) + 0.5) / 255.0
+
+    with open(path, "w") as f:
+        for v, c in zip(verts, colors_u8):
+            f.write("v %.9g %.9g %.9g %.9g %.9g %.9g\n" % (v[0], v[1], v[2], enc(c[0]), enc(c[1]),
+                                                         enc(c[2])))
+        for t in faces:
+            f.write("f %d %d %d\n" % (t[0] + 1, t[1] + 1, t[2] + 1))
