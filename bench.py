@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Benchmark of the FoundationPose B200 runtime: register throughput.
+
+Workload (synthetic stand-in for BOP YCB-V): one 640x480
+RGB-D frame + mask rendered from a ground-truth pose of a seeded 50k-triangle
+displaced sphere with per-vertex colours; register = 252 hypotheses, 5
+RefineNet iterations, ScoreNet over all 252, FP16, batch_size 252; weights are
+a seeded random init of the RefineNet/ScoreNet architecture (no checkpoint is
+available offline). One step = one fp_register_frame call through the C ABI.
+
+  value   hypotheses/s over all ranks with the frame already in HBM
+  e2e     same metric with pinned host frame buffers (H2D + pose D2H inside)
+  roofline  the tensor-core GEMM kernel: algorithmic FLOPs / CUDA-event time
+  cpu_baseline  the CPU restatement (oracle) + torch CPU networks, bounded sample
+
+Multi-GPU (torchrun): every rank registers its own frame (replicas, weak
+scaling); timing is the max over ranks. `--impl reference` times the CPU
+implementation of the same path (reference CPU preprocessing from oracle/_ref,
+CPU oracle for render/pack/pose kernels, torch fp32 networks on all host cores).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "foundation-pose-inference-library_b200"
+sys.path.insert(0, str(PKG / "python"))
+
+N_HYP = 252
+N_ITERS = 5
+W, H = 640, 480
+FP16 = 2
+METRIC = "register hypotheses/s (252 hyp, 5 refine iters + ScoreNet, 640x480, FP16)"
+WORKLOAD = "configs[1]: register, 50k-tri displaced sphere, 640x480 RGB-D+mask, 252 hyp, 5 iters, batch 252, FP16"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Scene
+# ---------------------------------------------------------------------------
+
+def build_scene(workdir: Path, seed: int):
+    from fp_b200 import synthetic as syn
+    from fp_b200.weights import make_default_packs
+
+    mesh = syn.displaced_sphere(seed)
+    obj = workdir / "object.obj"
+    with open(obj, "w") as f:
+        for v, c in zip(mesh.vertices, mesh.colors):
+            enc = [1.0 if x >= 255 else (float(x) + 0.5) / 255.0 for x in c]
+            f.write("v %.9g %.9g %.9g %.9g %.9g %.9g\n" % (v[0], v[1], v[2], *enc))
+        for t in mesh.faces:
+            f.write("f %d %d %d\n" % (t[0] + 1, t[1] + 1, t[2] + 1))
+    refine, score = make_default_packs(workdir / "weights", seed=0)
+    rng = np.random.default_rng(seed + 17)
+    gt = syn.random_pose(rng, dist=(0.65, 0.75), lateral=0.03)
+    return mesh, obj, refine, score, gt
+
+
+def render_frame(mesh, gt):
+    from fp_b200 import synthetic as syn
+    from fp_b200.kernels import FpkLibrary
+
+    fpk = FpkLibrary()
+    normals = syn.vertex_normals(mesh.vertices, mesh.faces)
+    rgb, depth = syn.render_frame_gpu(fpk, mesh, normals, gt, syn.K_640, W, H)
+    mask = (depth > 0).astype(np.uint8)
+    return rgb, depth, mask
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, path: Path):
+        self.path = path
+        self.proc = None
+        try:
+            self.fh = open(path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", str(gpu_index), "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU implementation (oracle + reference CPU functions + torch CPU networks)
+# ---------------------------------------------------------------------------
+
+def cpu_register_sample(n_sample: int, mesh, rgb, depth, mask, refine_pack, score_pack,
+                        iters: int = N_ITERS) -> float:
+    """Seconds for n_sample hypotheses through preprocess + `iters` refine
+    passes + one score pass on the host (one pass each over the sample)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import torch
+    from fp_b200.weights import read_pack
+    from fp_net_ref import NetRef
+    from oracle_lib import REF_CPU_SO, Oracle, RefCpu
+
+    from fp_b200 import synthetic as syn
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    o = Oracle()
+    cfg = o.config()
+    k4 = np.array([600.0, 600.0, 320.0, 240.0], np.float32)
+    center, diameter, verts = o.mesh_center_diameter(mesh.vertices)
+    normals = o.vertex_normals(verts, mesh.faces)
+    colors = (mesh.colors.astype(np.float32) / np.float32(255.0)).astype(np.float32)
+    nr = NetRef(read_pack(refine_pack)[1])
+    ns = NetRef(read_pack(score_pack)[1])
+    t0 = time.perf_counter()
+    if REF_CPU_SO.is_file():
+        filt = RefCpu().preprocess_depth(depth)  # the reference's own CPU preprocessing
+    else:
+        filt = o.preprocess_cpu(depth, cfg)
+    xyz = o.depth_to_xyz(filt, k4, cfg)
+    tr = o.initial_translation(filt, mask, k4, cfg)
+    rots = o.rotation_grid()[:n_sample]
+    poses = o.seed_poses(rots, tr)
+    for it in range(iters + 1):
+        boxes = o.crop_boxes(poses, k4, diameter, cfg)
+        rr, rx, _ = o.render(verts, normals, colors, mesh.faces, poses, boxes, k4, cfg)
+        thr = cfg.depth_min if it < iters else 0.1
+        a, b = o.pack(rgb, xyz, rr, rx, poses, boxes, diameter, thr, cfg)
+        A, B = torch.from_numpy(a), torch.from_numpy(b)
+        if it < iters:
+            dt, dr = nr.refine(A, B)
+            poses = o.apply_deltas(poses, dt.numpy(), dr.numpy(), diameter, cfg)
+        else:
+            scores = ns.score(A, B).numpy()
+            o.select_best(poses, scores, center)
+    return time.perf_counter() - t0
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    work = Path(tempfile.mkdtemp(prefix="fpbench_ref_"))
+    mesh, obj, refine, score, gt = build_scene(work, seed=args.seed)
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle_lib import Oracle
+    from fp_b200 import synthetic as syn
+
+    # The frame comes from the CPU oracle renderer (no GPU on this arm).
+    o = Oracle()
+    c, d, verts = o.mesh_center_diameter(mesh.vertices)
+    normals = o.vertex_normals(verts, mesh.faces)
+    cfg = o.config(input_width=W, input_height=H)
+    k4 = np.array([600.0, 600.0, 320.0, 240.0], np.float32)
+    gt_c = gt.copy()
+    rgbf, xyz, _ = o.render(verts, normals, (mesh.colors / np.float32(255.0)).astype(np.float32),
+                            mesh.faces, gt_c.reshape(1, 16), np.array([[0, 0, W, H]], np.float32), k4, cfg)
+    rgb = (np.clip(rgbf[0], 0, 1) * 255 + 0.5).astype(np.uint8)
+    depth = xyz[0, ..., 2].astype(np.float32)
+    mask = (depth > 0).astype(np.uint8)
+    n_sample = args.cpu_sample
+    for _ in range(args.warmup if args.warmup < 1 else 1):
+        cpu_register_sample(n_sample, mesh, rgb, depth, mask, refine, score, iters=1)
+    times = [cpu_register_sample(n_sample, mesh, rgb, depth, mask, refine, score) for _ in range(args.steps)]
+    per = statistics.mean(times)
+    value = n_sample / per
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "hyp/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1000.0,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "sample": f"{n_sample} of {N_HYP} hypotheses"},
+        "cpu_baseline": {"value": value, "unit": "hyp/s", "cores": cores, "kind": "port",
+                         "sample": f"{n_sample} hypotheses x (preprocess + 5 refine + 1 score pass); "
+                                   "reference CPU preprocessDepth (oracle/_ref), CPU oracle render/pack/pose, "
+                                   "torch fp32 networks"},
+        "e2e": {"value": value, "unit": "hyp/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"bf16": d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), "hbm": d.get("hbm_gbs"),
+                "note": "of measured"}
+    return {"bf16": 1590.0, "hbm": 6650.0, "note": "of fallback"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--cpu-sample", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--track-frames", type=int, default=50)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+
+    import foundation_pose_nvidia as fpn
+    from foundation_pose_nvidia.bindings import CreateOptions, PoseResult
+    from fp_b200.kernels import FpkLibrary
+
+    work = Path(tempfile.mkdtemp(prefix=f"fpbench_{rank}_"))
+    mesh, obj, refine, score, gt = build_scene(work, seed=args.seed + rank)
+    rgb, depth, mask = render_frame(mesh, gt)
+
+    lib = fpn.load_library(print_build_info=False)
+    fpk = FpkLibrary()
+    fpk.lib.fpk_profile_enable.argtypes = [C.c_int]
+    fpk.lib.fpk_profile_read.argtypes = [C.c_void_p] * 4
+    cfg = lib.default_config()
+    cfg.n_hypotheses, cfg.n_refine_iters, cfg.batch_size = N_HYP, N_ITERS, N_HYP
+    cfg.tensorrt_precision = FP16
+    cfg.max_image_width, cfg.max_image_height = W, H
+    strs = [str(obj).encode(), str(refine).encode(), str(score).encode(), str(work).encode()]
+    opts = CreateOptions(strs[0], local, 1.0, strs[1], strs[2], strs[3])
+    err = C.create_string_buffer(2048)
+    h = lib.cdll.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
+    if not h:
+        raise SystemExit(f"fp_create failed: {err.value.decode()}")
+    if lib.cdll.fp_prepare(h, N_HYP, err, len(err)) != 0:
+        raise SystemExit(f"fp_prepare failed: {err.value.decode()}")
+
+    dev = torch.device("cuda", local)
+    d_rgb, d_depth, d_mask = (torch.from_numpy(x).to(dev) for x in (rgb, depth, mask))
+    p_rgb, p_depth, p_mask = (torch.from_numpy(x).pin_memory() for x in (rgb, depth, mask))
+    K = np.array([[600, 0, 320], [0, 600, 240], [0, 0, 1]], np.float32)
+    dev_view = fpn.RgbdFrame(d_rgb, d_depth, K, d_mask).to_image_view(with_mask=True)
+    host_view = fpn.RgbdFrame(p_rgb.numpy(), p_depth.numpy(), K, p_mask.numpy()).to_image_view(with_mask=True)
+    result = PoseResult()
+
+    def register(v):
+        if lib.cdll.fp_register_frame(h, C.byref(v), -1, -1, C.byref(result), err, len(err)) != 0:
+            raise SystemExit(f"fp_register_frame failed: {err.value.decode()}")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local, work / "clocks.csv")  # samples warm-up + timed region (GPU busy)
+    for _ in range(args.warmup):
+        register(dev_view)
+    torch.cuda.synchronize()
+
+    # Timed region: device-resident frame.
+    stream = torch.cuda.current_stream(dev)
+    fpk.lib.fpk_profile_reset()
+    fpk.lib.fpk_profile_enable(1)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        register(dev_view)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    fpk.lib.fpk_profile_enable(0)
+    ms_tot = (C.c_double * 5)()
+    work_tot = (C.c_double * 5)()
+    timed = (C.c_longlong * 5)()
+    launches = (C.c_longlong * 5)()
+    fpk.lib.fpk_profile_read(ms_tot, work_tot, timed, launches)
+    ms_per_step = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    value = world * N_HYP / (ms_per_step / 1000.0)
+    pose_dev = np.array(result.pose_row_major, np.float32).reshape(4, 4)
+
+    # End-to-end: pinned host buffers, H2D of the frame and D2H of the pose inside each step.
+    for _ in range(2):
+        register(host_view)
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        register(host_view)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps)
+    pose_host = np.array(result.pose_row_major, np.float32).reshape(4, 4)
+
+    # Track rate on the same estimator (B=1, 2 iterations), device-resident frame.
+    track_view = fpn.RgbdFrame(d_rgb, d_depth, K).to_image_view(with_mask=False)
+    for _ in range(5):
+        lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.track_frames):
+        if lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err)) != 0:
+            raise SystemExit(f"fp_track_frame failed: {err.value.decode()}")
+    torch.cuda.synchronize()
+    track_hz = args.track_frames / (time.perf_counter() - t0)
+    lib.cdll.fp_destroy(h)
+
+    if rank == 0:
+        pk = peaks()
+        gemm_ms, gemm_flops, gemm_n = ms_tot[0], work_tot[0], timed[0]
+        achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+        render_ms, render_bytes = ms_tot[1], work_tot[1]
+        cpu_base = None
+        if not args.no_cpu_baseline and world == 1:
+            t = cpu_register_sample(args.cpu_sample, mesh, rgb, depth, mask, refine, score)
+            cpu_base = {"value": args.cpu_sample / t, "unit": "hyp/s", "cores": os.cpu_count() or 1,
+                        "kind": "port",
+                        "sample": f"{args.cpu_sample} hypotheses x (preprocess + 5 refine + 1 score pass) "
+                                  "on the host: reference CPU preprocessDepth, CPU oracle render/pack/pose, "
+                                  "torch fp32 networks"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "hyp/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded scene; random-init weights)",
+            "config": {"workload": WORKLOAD, "global_batch": N_HYP * world, "register_ms": ms_per_step,
+                       "l2": "not flushed: each register streams ~2.5 GB of activations (> 126 MB L2)",
+                       "parallelism": f"replicas x{world} (one register per GPU)"},
+            "e2e": {"value": world * N_HYP / (e2e_ms / 1000.0), "unit": "hyp/s",
+                    "h2d_bytes_per_step": int(rgb.nbytes + depth.nbytes + mask.nbytes),
+                    "d2h_bytes_per_step": 72, "register_ms": e2e_ms},
+            "roofline": {"kernel": "gemmKernel (tcgen05 implicit-GEMM conv/linear)", "bound": "tensor",
+                         "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s",
+                         "frac": (achieved / pk["bf16"]) if achieved else None, "peak_note": pk["note"] + " (sustained bf16)",
+                         "traffic": None, "launches_timed": gemm_n, "gemm_ms_per_step": gemm_ms / args.steps,
+                         "gemm_tflop_per_step": gemm_flops / args.steps / 1e12},
+            "render_pack": {"ms_per_step": render_ms / args.steps,
+                            "achieved_gbs": render_bytes / (render_ms / 1000.0) / 1e9 if render_ms > 0 else None,
+                            "peak_gbs": pk["hbm"]},
+            "stage_ms_per_step": {k: ms_tot[i] / args.steps for i, k in
+                                  enumerate(["gemm", "render_pack", "attention", "other", "preprocess"])},
+            "gpu_launches": int(sum(launches[i] for i in range(5))),
+            "track_hz": track_hz,
+            "clocks": clocks,
+            "cpu_baseline": cpu_base,
+            "pose_host_equals_device": bool(np.array_equal(pose_dev, pose_host)),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

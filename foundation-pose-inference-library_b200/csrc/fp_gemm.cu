@@ -27,6 +27,7 @@
 #include <type_traits>
 #include <unordered_map>
 
+#include "fp_profile.hpp"
 #include "fpk.h"
 
 namespace fpb {
@@ -547,6 +548,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   }
   const int tiles = pl.m_tiles * pl.n_tiles;
   const int grid = tiles < numSms() ? tiles : numSms();
+  prof::countLaunch(prof::kGemm);
   gemmKernel<T, BN><<<grid, kThreads, smem, stream>>>(d, pl, map);
   return checkLaunch("gemmKernel");
 }

@@ -16,6 +16,7 @@
 #include <cstdint>
 
 #include "fp_net_kernels.cuh"
+#include "fp_profile.hpp"
 
 namespace fpb {
 namespace net {
@@ -445,19 +446,27 @@ __global__ void convertKernel(const float* __restrict__ in, T* __restrict__ out,
 cudaError_t launchAttention(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s) {
   const size_t smem = 3 * kQBlock * kLd * 2;
   const dim3 grid((a.seq_len + kQBlock - 1) / kQBlock, layers * a.heads, n_seq);
-  if (bf16) {
+  prof::countLaunch(prof::kAttention);
+  static int attr_mask = 0;  // one bit per device: dynamic smem opt-in done
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 31 && !(attr_mask & (1 << dev))) {
     cudaFuncSetAttribute(attentionKernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    attentionKernel<__nv_bfloat16><<<grid, 128, smem, s>>>(a);
-  } else {
     cudaFuncSetAttribute(attentionKernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
+    attr_mask |= 1 << dev;
+  }
+  if (bf16) {
+    attentionKernel<__nv_bfloat16><<<grid, 128, smem, s>>>(a);
+  } else {
     attentionKernel<__half><<<grid, 128, smem, s>>>(a);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launchLayerNorm(const LnArgs& a, bool bf16, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
   const int grid = static_cast<int>((a.rows + 31) / 32);
   if (bf16) {
     layerNormKernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a);
@@ -469,6 +478,7 @@ cudaError_t launchLayerNorm(const LnArgs& a, bool bf16, cudaStream_t s) {
 
 cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int seq_len, int n_seq,
                             float* out, bool bf16, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
   if (bf16) {
     tokenMeanKernel<__nv_bfloat16><<<n_seq, 256, 0, s>>>(in, plane_stride, seq_len, out);
   } else {
@@ -479,18 +489,21 @@ cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int
 
 cudaError_t launchLinearF32(const float* x, const float* w, const float* b, float* y, int m, int n,
                             int k, bool relu, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
   const dim3 grid((n + 31) / 32, (m + 31) / 32);
   linearF32Kernel<<<grid, 256, 0, s>>>(x, w, b, y, m, n, k, relu ? 1 : 0);
   return cudaGetLastError();
 }
 
 cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
   smallAttentionKernel<<<dim3(len, 4), 128, static_cast<size_t>(len) * sizeof(float), s>>>(qkv, len, out);
   return cudaGetLastError();
 }
 
 cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n, int H, int W,
                              void* dst, long long plane_stride, bool bf16, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
   const long long total = 2LL * n * H * W;
   const unsigned grid = static_cast<unsigned>((total + 255) / 256);
   if (bf16) {
@@ -504,6 +517,7 @@ cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n
 }
 
 cudaError_t launchConvert(const float* in, void* out, long long n, bool bf16, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
   const unsigned grid = static_cast<unsigned>((n + 255) / 256);
   if (bf16) {
     convertKernel<__nv_bfloat16><<<grid, 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), n);

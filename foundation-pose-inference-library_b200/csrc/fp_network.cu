@@ -23,6 +23,7 @@
 
 #include "fp_net_kernels.cuh"
 #include "fp_network.hpp"
+#include "fp_profile.hpp"
 
 namespace fpb {
 
@@ -155,8 +156,10 @@ class Network {
   Network(const WeightPack& pack, bool bf16, std::vector<void*>& allocs)
       : bf16_(bf16), allocs_(allocs), arch_(pack.arch) {
     // Encoder.
-    conv("encA.conv1", pack, s2dTaps(pack.at("encA.conv1.w"), 64, 6, 7, 8), 64, 32, 16, offsets(4, kStemGrid));
-    conv("encA.conv2", pack, s2dTaps(pack.at("encA.conv2.w"), 128, 64, 3, 64), 128, 256, 4, offsets(2, kG40));
+    conv("encA.conv1", pack, s2dTaps(pack.at("encA.conv1.w"), 64, 6, 7, 8), 64, 32, 16, offsets(4, kStemGrid),
+         2.0 * 64 * 49 * 6);
+    conv("encA.conv2", pack, s2dTaps(pack.at("encA.conv2.w"), 128, 64, 3, 64), 128, 256, 4, offsets(2, kG40),
+         2.0 * 128 * 9 * 64);
     for (const char* r : {"encA.res1", "encA.res2"}) {
       plain3(std::string(r) + ".c1", pack, 128, kG40);
       plain3(std::string(r) + ".c2", pack, 128, kG40);
@@ -165,7 +168,8 @@ class Network {
       plain3(std::string(r) + ".c1", pack, 256, kG40);
       plain3(std::string(r) + ".c2", pack, 256, kG40);
     }
-    conv("encAB.conv", pack, s2dTaps(pack.at("encAB.conv.w"), 512, 256, 3, 256), 512, 1024, 4, offsets(2, kG20));
+    conv("encAB.conv", pack, s2dTaps(pack.at("encAB.conv.w"), 512, 256, 3, 256), 512, 1024, 4, offsets(2, kG20),
+         2.0 * 512 * 9 * 256);
     for (const char* r : {"encAB.res3", "encAB.res4"}) {
       plain3(std::string(r) + ".c1", pack, 512, kG20);
       plain3(std::string(r) + ".c2", pack, 512, kG20);
@@ -246,8 +250,9 @@ class Network {
   }
 
   void conv(const std::string& name, const WeightPack& pack, const std::vector<float>& taps_w,
-            int cout, int cin, int taps, const std::vector<int>& offs) {
+            int cout, int cin, int taps, const std::vector<int>& offs, double flops_per_row) {
     ConvLayer c;
+    c.flops_per_row = flops_per_row;
     c.w = uploadHalf(chunkMajor(taps_w, cout, taps, cin));
     c.bias = upload(pack.at(name + ".b"));
     c.cin = cin;
@@ -261,7 +266,7 @@ class Network {
     std::vector<int> offs;
     for (int ky = 0; ky < 3; ++ky)
       for (int kx = 0; kx < 3; ++kx) offs.push_back((ky - 1) * grid + (kx - 1));
-    conv(name, pack, plainTaps(pack.at(name + ".w"), ch, ch, 3), ch, ch, 9, offs);
+    conv(name, pack, plainTaps(pack.at(name + ".w"), ch, ch, 3), ch, ch, 9, offs, 2.0 * ch * 9 * ch);
   }
 
   ConvLayer linear(const std::vector<float>& w, const std::vector<float>& b, int cout, int cin) {
@@ -271,6 +276,7 @@ class Network {
     c.cin = cin;
     c.cout = cout;
     c.taps = 1;
+    c.flops_per_row = 2.0 * cout * cin;
     return c;
   }
 
@@ -407,6 +413,8 @@ void NetworkRunner::gemm(const ConvLayer& L, const Planar& a, long long a_row0, 
   d.pos = pos;
   d.dtype = dtype();
   d.error_flag = err_;
+  const double valid_rows = static_cast<double>(rows / img_rows) * valid_h * valid_w;
+  prof::Scope scope(prof::kGemm, valid_rows * L.flops_per_row, s);
   if (fpk_gemm(&d, s) != 0) throw std::runtime_error(fpk_last_error());
 }
 
@@ -463,7 +471,10 @@ void NetworkRunner::refine(int count, int first_chunk, float* delta_t, float* de
   at.seq_len = kTokens;
   at.heads = 4;
   at.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
-  check(net::launchAttention(at, 2, count, bf, s), "attention");
+  {
+    prof::Scope scope(prof::kAttention, 2.0 * 4 * count * 4.0 * kTokens * kTokens * 128, s);
+    check(net::launchAttention(at, 2, count, bf, s), "attention");
+  }
   float* outs[2] = {delta_t, delta_r};
   const char* heads[2] = {"trans", "rot"};
   for (int z = 0; z < 2; ++z) {
@@ -504,7 +515,10 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
   at.seq_len = kTokens;
   at.heads = 4;
   at.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
-  check(net::launchAttention(at, 1, n, bf, s), "attention");
+  {
+    prof::Scope scope(prof::kAttention, 1.0 * 4 * n * 4.0 * kTokens * kTokens * 128, s);
+    check(net::launchAttention(at, 1, n, bf, s), "attention");
+  }
   gemm(net.L("out_proj"), a.att, 0, T, a.y1, FPK_DST_SAME, t, 1, t, 1, false, nullptr, 0, 0, 1, 0, nullptr, s);
   check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, n, a.feat, bf, s), "token mean");
   // Attention across the n hypotheses (fp32), then the score head.

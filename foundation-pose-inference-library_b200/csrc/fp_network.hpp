@@ -46,6 +46,7 @@ struct ConvLayer {
   float* bias = nullptr;   // [cout]
   int cin = 0, cout = 0, taps = 0;
   int tap_off[FPK_GEMM_MAX_TAPS] = {};
+  double flops_per_row = 0.0;  // algorithmic FLOPs per valid output row (un-padded op)
 };
 
 class Network;

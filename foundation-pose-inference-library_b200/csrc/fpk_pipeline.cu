@@ -19,6 +19,7 @@
 #include <type_traits>
 
 #include "fp_device.cuh"
+#include "fp_profile.hpp"
 #include "fpk.h"
 
 namespace fpb {
@@ -1020,6 +1021,15 @@ int launchRender(RenderArgs& a, cudaStream_t stream) {
     }
     attr_done_mask |= 1 << dev;
   }
+  // Algorithmic bytes: mesh once, the frame once (rgb + depth) when packing,
+  // and the outputs (NHWC fp32 rgb+xyz, or both packed network inputs).
+  const double px = static_cast<double>(a.n) * a.p.input_width * a.p.input_height;
+  const double elt = kOut == RenderOut::kNhwc ? 0.0 : (kOut == RenderOut::kS2dF32 ? 4.0 : 2.0);
+  const double bytes = a.mesh.n_vertices * 36.0 + a.mesh.n_faces * 12.0 +
+                       (kOut == RenderOut::kNhwc ? px * 24.0
+                                                 : px * 12.0 * elt + a.img_w * static_cast<double>(a.img_h) * 7.0);
+  prof::countLaunch(prof::kRender);
+  prof::Scope scope(prof::kRender, bytes, stream);
   renderKernel<kOut><<<dim3(nb, a.n), kRenderThreads, smem, stream>>>(a);
   return checkLaunch("renderKernel");
 }
@@ -1075,6 +1085,8 @@ int fpk_preprocess(const float* depth_raw, const uint8_t* mask, int width, int h
     if (e != cudaSuccess) return fail(std::string("fpk_preprocess memset: ") + cudaGetErrorString(e));
   }
   const dim3 grid((width + kPreTileW - 1) / kPreTileW, (height + kPreTileH - 1) / kPreTileH);
+  prof::countLaunch(prof::kPreprocess);
+  prof::Scope scope(prof::kPreprocess, 20.0 * width * height, s);
   preprocessKernel<<<grid, dim3(32, 8), 0, s>>>(depth_raw, mask, width, height, k, *p,
                                                 depth_filtered, eroded, xyz, stats);
   return checkLaunch("preprocessKernel");
@@ -1086,6 +1098,7 @@ int fpk_seed_poses(const int32_t* stats, const float* rotations, int n, fpk_intr
   if (stats == nullptr || (n > 0 && (rotations == nullptr || poses == nullptr))) {
     return fail("fpk_seed_poses: null buffer");
   }
+  prof::countLaunch(prof::kPreprocess);
   seedPosesKernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(stats, rotations, n, k, *p,
                                                                      t0, poses);
   return checkLaunch("seedPosesKernel");
@@ -1095,6 +1108,7 @@ int fpk_crop_boxes(const float* poses, int n, fpk_intrinsics_t k, float diameter
                    const fpk_params_t* p, float* boxes, void* stream) {
   if (validateParams(p) != 0) return 1;
   if (n <= 0) return fail("fpk_crop_boxes: n must be positive");
+  prof::countLaunch(prof::kOther);
   cropBoxesKernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       poses, n, k, diameter, p->crop_ratio, reinterpret_cast<float4*>(boxes));
   return checkLaunch("cropBoxesKernel");
@@ -1141,6 +1155,7 @@ int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, int hei
   a.img_h = height;
   a.invalid_threshold = invalid_depth_threshold;
   const long long total = static_cast<long long>(n) * p->input_width * p->input_height;
+  prof::countLaunch(prof::kOther);
   packNchwKernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0,
                    static_cast<cudaStream_t>(stream)>>>(a, rend_rgb, rend_xyz, net_rendered,
                                                         net_observed);
@@ -1193,6 +1208,7 @@ int fpk_apply_deltas(float* poses, const float* delta_t, const float* delta_r, i
                      float diameter, const fpk_params_t* p, void* stream) {
   if (validateParams(p) != 0) return 1;
   if (n <= 0) return fail("fpk_apply_deltas: n must be positive");
+  prof::countLaunch(prof::kOther);
   applyDeltasKernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       poses, delta_t, delta_r, n, diameter, p->rotation_normalizer_rad);
   return checkLaunch("applyDeltasKernel");
@@ -1201,6 +1217,7 @@ int fpk_apply_deltas(float* poses, const float* delta_t, const float* delta_r, i
 int fpk_select_best(const float* poses, const float* scores, int n, const float* center3,
                     float* result, void* stream) {
   if (n <= 0 || center3 == nullptr) return fail("fpk_select_best: bad arguments");
+  prof::countLaunch(prof::kOther);
   selectBestKernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       poses, scores, n, center3[0], center3[1], center3[2], result);
   return checkLaunch("selectBestKernel");

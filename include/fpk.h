@@ -205,6 +205,19 @@ FP_API int fpk_net_score(fpk_net_t* net, const float* rendered, const float* obs
 /* Device error flag of the pipelined kernels: 0 = ok (non-zero after a wait timed out). */
 FP_API int fpk_net_error(fpk_net_t* net, int* host_flag);
 
+/* ---------------------------------------------------------------------------
+ * Benchmark instrumentation (no counterpart in the reference, which has no
+ * tracing). Stages: 0 tensor-core GEMM, 1 fused render+pack / render,
+ * 2 attention, 3 other network kernels, 4 frame preprocess.
+ * fpk_profile_enable(1) makes every stage record a CUDA event pair on its own
+ * stream plus its algorithmic work (GEMM: FLOPs of the un-padded convolution or
+ * matmul; render: bytes of mesh + frame read and network input written).
+ * Launch counts are always kept. fpk_profile_read fills arrays of 5 per stage
+ * (any may be NULL) and returns 5. */
+FP_API void fpk_profile_enable(int enable);
+FP_API void fpk_profile_reset(void);
+FP_API int fpk_profile_read(double* ms, double* work, long long* timed, long long* launches);
+
 #ifdef __cplusplus
 }
 #endif
