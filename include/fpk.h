@@ -205,6 +205,23 @@ FP_API int fpk_net_score(fpk_net_t* net, const float* rendered, const float* obs
 /* Device error flag of the pipelined kernels: 0 = ok (non-zero after a wait timed out). */
 FP_API int fpk_net_error(fpk_net_t* net, int* host_flag);
 
+/* Allocation-free initial translation. No counterpart in the reference: it is
+ * the same chain as fpk_preprocess + fpk_seed_poses (the reference's
+ * runDepthPreprocess + runInitialTranslation) for callers that may not allocate
+ * device memory -- real-time loops and safety-reviewed deployments that freeze
+ * their memory at start-up, and plugin hosts that own every buffer. The caller
+ * passes the raw depth and mask (device) and receives t0 [3] (device); the
+ * filtered depth and the depth histogram live in fixed device arrays built
+ * into the library (about 3.8 MiB on every GPU that loads it, until exit).
+ * Frames larger than FPK_NOALLOC_MAX_PIXELS (1280x720) are rejected with an
+ * error. The first call on a device looks up the arrays' device addresses and
+ * should come before any stream capture. All calls share the arrays: calls that
+ * overlap on the GPU race and must be serialised by the caller. */
+#define FPK_NOALLOC_MAX_PIXELS (1280 * 720)
+FP_API int fpk_initial_translation_noalloc(const float* depth_raw, const uint8_t* mask, int width,
+                                           int height, fpk_intrinsics_t k, const fpk_params_t* p,
+                                           float* t0, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Benchmark instrumentation (no counterpart in the reference, which has no
  * tracing). Stages: 0 tensor-core GEMM, 1 fused render+pack / render,
