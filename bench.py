@@ -248,6 +248,7 @@ def main() -> None:
     ap.add_argument("--cpu-sample", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--track-frames", type=int, default=50)
+    ap.add_argument("--e2e-steps", type=int, default=None, help="host-buffer steps (default: --steps)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
@@ -302,16 +303,11 @@ def main() -> None:
         if lib.cdll.fp_register_frame(h, C.byref(v), -1, -1, C.byref(result), err, len(err)) != 0:
             raise SystemExit(f"fp_register_frame failed: {err.value.decode()}")
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    from fp_b200.dist_utils import barrier
+    from fp_b200.dist_utils import max_over_ranks as _max
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max(x, dev)
 
     sampler = ClockSampler(local, work / "clocks.csv")  # samples warm-up + timed region (GPU busy)
     for _ in range(args.warmup):
@@ -343,31 +339,36 @@ def main() -> None:
     pose_dev = np.array(result.pose_row_major, np.float32).reshape(4, 4)
 
     # End-to-end: pinned host buffers, H2D of the frame and D2H of the pose inside each step.
-    for _ in range(2):
-        register(host_view)
-    barrier()
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(args.steps):
-        register(host_view)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps)
-    pose_host = np.array(result.pose_row_major, np.float32).reshape(4, 4)
+    e2e_steps = args.steps if args.e2e_steps is None else args.e2e_steps
+    e2e_ms, pose_host = float("nan"), None
+    if e2e_steps > 0:
+        for _ in range(2):
+            register(host_view)
+        barrier()
+        torch.cuda.synchronize()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(e2e_steps):
+            register(host_view)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e2.elapsed_time(e3) / e2e_steps)
+        pose_host = np.array(result.pose_row_major, np.float32).reshape(4, 4)
 
     # Track rate on the same estimator (B=1, 2 iterations), device-resident frame.
     track_view = fpn.RgbdFrame(d_rgb, d_depth, K).to_image_view(with_mask=False)
-    for _ in range(5):
-        lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err))
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(args.track_frames):
-        if lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err)) != 0:
-            raise SystemExit(f"fp_track_frame failed: {err.value.decode()}")
-    torch.cuda.synchronize()
-    track_hz = args.track_frames / (time.perf_counter() - t0)
+    track_hz = None
+    if args.track_frames > 0:
+        for _ in range(5):
+            lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.track_frames):
+            if lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err)) != 0:
+                raise SystemExit(f"fp_track_frame failed: {err.value.decode()}")
+        torch.cuda.synchronize()
+        track_hz = args.track_frames / (time.perf_counter() - t0)
     lib.cdll.fp_destroy(h)
 
     if rank == 0:
@@ -390,7 +391,7 @@ def main() -> None:
             "config": {"workload": WORKLOAD, "global_batch": N_HYP * world, "register_ms": ms_per_step,
                        "l2": "not flushed: each register streams ~2.5 GB of activations (> 126 MB L2)",
                        "parallelism": f"replicas x{world} (one register per GPU)"},
-            "e2e": {"value": world * N_HYP / (e2e_ms / 1000.0), "unit": "hyp/s",
+            "e2e": {"value": world * N_HYP / (e2e_ms / 1000.0) if e2e_steps > 0 else None, "unit": "hyp/s",
                     "h2d_bytes_per_step": int(rgb.nbytes + depth.nbytes + mask.nbytes),
                     "d2h_bytes_per_step": 72, "register_ms": e2e_ms},
             "roofline": {"kernel": "gemmKernel (tcgen05 implicit-GEMM conv/linear)", "bound": "tensor",
@@ -407,7 +408,7 @@ def main() -> None:
             "track_hz": track_hz,
             "clocks": clocks,
             "cpu_baseline": cpu_base,
-            "pose_host_equals_device": bool(np.array_equal(pose_dev, pose_host)),
+            "pose_host_equals_device": None if pose_host is None else bool(np.array_equal(pose_dev, pose_host)),
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -22,6 +22,7 @@
 #include "foundation_pose_nvidia/foundation_pose.hpp"
 #include "foundation_pose_nvidia/types.hpp"
 #include "fp_host.hpp"
+#include "fpk.h"
 
 namespace foundation_pose_nvidia {
 
@@ -519,3 +520,58 @@ Mesh reconstructReferenceMesh(std::span<const ModelFreeReferenceView> refs, cons
 
 }  // namespace fpb_host
 }  // namespace foundation_pose_nvidia
+
+namespace fpb {
+int fail(const std::string& msg);
+}
+
+extern "C" int fpk_load_mesh(const char* path, float mesh_unit_scale, int* n_vertices, int* n_faces,
+                             float* vertices, float* normals, uint8_t* colors, int32_t* faces,
+                             float* center3, float* diameter) {
+  using namespace foundation_pose_nvidia;
+  try {
+    if (path == nullptr || n_vertices == nullptr || n_faces == nullptr) {
+      return fpb::fail("fpk_load_mesh: path and count outputs are required");
+    }
+    Mesh mesh = loadMesh(path);
+    if (mesh_unit_scale > 0.0f && mesh_unit_scale != 1.0f) {
+      for (Vec3f& v : mesh.vertices) v = v * mesh_unit_scale;
+    }
+    const PreprocessedMesh pm = preprocessMesh(mesh, Config{});
+    const Mesh& m = pm.centered_mesh;
+    *n_vertices = static_cast<int>(m.vertices.size());
+    *n_faces = static_cast<int>(m.faces.size());
+    if (vertices != nullptr) {
+      for (std::size_t i = 0; i < m.vertices.size(); ++i) {
+        vertices[3 * i] = m.vertices[i].x;
+        vertices[3 * i + 1] = m.vertices[i].y;
+        vertices[3 * i + 2] = m.vertices[i].z;
+        const Vec3f n = i < m.normals.size() ? m.normals[i] : Vec3f{0.0f, 0.0f, 1.0f};
+        if (normals != nullptr) {
+          normals[3 * i] = n.x;
+          normals[3 * i + 1] = n.y;
+          normals[3 * i + 2] = n.z;
+        }
+        const Vec3u8 c = i < m.vertex_colors.size() ? m.vertex_colors[i] : Vec3u8{};
+        if (colors != nullptr) {
+          colors[3 * i] = c.r;
+          colors[3 * i + 1] = c.g;
+          colors[3 * i + 2] = c.b;
+        }
+      }
+    }
+    if (faces != nullptr) {
+      for (std::size_t i = 0; i < m.faces.size(); ++i)
+        for (int k = 0; k < 3; ++k) faces[3 * i + k] = static_cast<int32_t>(m.faces[i][k]);
+    }
+    if (center3 != nullptr) {
+      center3[0] = pm.center.x;
+      center3[1] = pm.center.y;
+      center3[2] = pm.center.z;
+    }
+    if (diameter != nullptr) *diameter = pm.diameter;
+    return 0;
+  } catch (const std::exception& e) {
+    return fpb::fail(e.what());
+  }
+}

@@ -121,6 +121,17 @@ FP_API int fpk_render_pack(const fpk_mesh_t* mesh, const float* poses, int n,
                            float invalid_depth_threshold, int dtype, void* net_input,
                            long long plane_stride, float* boxes, void* stream);
 
+/* Host-only mesh ingest: load an OBJ/PLY, scale by mesh_unit_scale, compute
+ * normals when missing, centre on the bounding-box centre and measure the
+ * diameter. Replaces loadMesh + preprocessMesh (reference src/mesh.cpp:577-680)
+ * as used by FoundationPose::createFromCadFile (src/foundation_pose.cpp:281-294).
+ * Call once with NULL arrays to get the counts, then again with arrays of
+ * n_vertices*3 floats (vertices, normals), n_vertices*3 bytes (colours) and
+ * n_faces*3 int32 (faces). center3 [3] and diameter receive the centring. */
+FP_API int fpk_load_mesh(const char* path, float mesh_unit_scale, int* n_vertices, int* n_faces,
+                         float* vertices, float* normals, uint8_t* colors, int32_t* faces,
+                         float* center3, float* diameter);
+
 /* R <- exp(tanh(dr)*norm)^T R; t += dt*diameter/2. Replaces applyPoseDeltasOnDevice
  * (reference src/cuda_pipeline.cu:513-547, 847-858). In place. */
 FP_API int fpk_apply_deltas(float* poses, const float* delta_t, const float* delta_r, int n,

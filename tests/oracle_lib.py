@@ -165,6 +165,7 @@ class RefCpu:
     def __init__(self, path: Path = REF_CPU_SO):
         if not path.is_file():
             raise FileNotFoundError(str(path))
+        self.path = path
         self.lib = C.CDLL(str(path))
         self.lib.refcpu_rotation_grid.restype = C.c_int
         self.lib.refcpu_preprocess_depth.restype = C.c_int
@@ -207,21 +208,36 @@ class RefCpu:
         return out
 
     def load_mesh(self, path: str):
-        nv, nf = C.c_int(0), C.c_int(0)
-        center = np.zeros(3, np.float32)
-        diam = C.c_float(0)
-        err = C.create_string_buffer(512)
-        rc = self.lib.refcpu_load_mesh(str(path).encode(), C.byref(nv), C.byref(nf), None, None,
-                                       None, None, ptr(center), C.byref(diam), err, 512)
-        if rc != 0:
-            raise RuntimeError(err.value.decode())
-        v = np.zeros((nv.value, 3), np.float32)
-        n = np.zeros((nv.value, 3), np.float32)
-        col = np.zeros((nv.value, 3), np.uint8)
-        f = np.zeros((nf.value, 3), np.uint32)
-        self.lib.refcpu_load_mesh(str(path).encode(), C.byref(nv), C.byref(nf), ptr(v), ptr(n),
-                                  ptr(col), ptr(f), ptr(center), C.byref(diam), err, 512)
-        return dict(vertices=v, normals=n, colors=col, faces=f, center=center, diameter=diam.value)
+        """Reference loadMesh + preprocessMesh. Runs in a fresh interpreter that
+        never imports numpy: the reference's iostream-based OBJ parser crashes
+        when numpy's libstdc++ locale state shares the process."""
+        import pickle
+        import subprocess
+        import sys
+
+        script = (
+            "import ctypes as C, pickle, sys\n"
+            f"lib = C.CDLL({str(self.path)!r})\n"
+            "nv, nf, d = C.c_int(0), C.c_int(0), C.c_float(0)\n"
+            "c = (C.c_float * 3)(); err = C.create_string_buffer(512)\n"
+            f"p = {str(path)!r}.encode()\n"
+            "rc = lib.refcpu_load_mesh(p, C.byref(nv), C.byref(nf), None, None, None, None, c, C.byref(d), err, 512)\n"
+            "if rc: sys.stdout.buffer.write(pickle.dumps(('err', err.value.decode()))); sys.exit(0)\n"
+            "v = (C.c_float * (3 * nv.value))(); n = (C.c_float * (3 * nv.value))()\n"
+            "col = (C.c_uint8 * (3 * nv.value))(); f = (C.c_uint32 * (3 * nf.value))()\n"
+            "lib.refcpu_load_mesh(p, C.byref(nv), C.byref(nf), v, n, col, f, c, C.byref(d), err, 512)\n"
+            "sys.stdout.buffer.write(pickle.dumps(('ok', bytes(v), bytes(n), bytes(col), bytes(f), bytes(c), d.value)))\n"
+        )
+        out = subprocess.run([sys.executable, "-c", script], capture_output=True, check=True).stdout
+        res = pickle.loads(out)
+        if res[0] != "ok":
+            raise RuntimeError(res[1])
+        _, v, n, col, f, c, diam = res
+        return dict(vertices=np.frombuffer(v, np.float32).reshape(-1, 3).copy(),
+                    normals=np.frombuffer(n, np.float32).reshape(-1, 3).copy(),
+                    colors=np.frombuffer(col, np.uint8).reshape(-1, 3).copy(),
+                    faces=np.frombuffer(f, np.uint32).reshape(-1, 3).copy(),
+                    center=np.frombuffer(c, np.float32).copy(), diameter=diam)
 
 
 class RefGpu:

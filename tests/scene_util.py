@@ -58,7 +58,13 @@ def make_scene(oracle, kind: str = "ellipsoid_small", seed: int = 0, width: int 
     center, diameter, centered = oracle.mesh_center_diameter(m.vertices)
     normals = oracle.vertex_normals(centered, m.faces)
     colors_f = (m.colors.astype(np.float32) / np.float32(255.0)).astype(np.float32)
-    K = syn.K_640 if width == 640 else syn.K_1280
+    if (width, height) == (640, 480):
+        K = syn.K_640
+    elif (width, height) == (1280, 720):
+        K = syn.K_1280
+    else:  # same field of view as the 640x480 camera
+        f = 600.0 * width / 640.0
+        K = np.array([[f, 0.0, width / 2.0], [0.0, f, height / 2.0], [0.0, 0.0, 1.0]], np.float32)
     k4 = np.array([K[0, 0], K[1, 1], K[0, 2], K[1, 2]], np.float32)
     pose = syn.random_pose(rng, dist=(0.6, 0.8), lateral=0.03)
     cfg = oracle.config(input_width=width, input_height=height)
