@@ -1,7 +1,10 @@
 """Generate golden vectors from the reference's own builds (test fixtures).
 
   python tests/golden/make_golden.py cpu   # needs oracle/_ref/libfpref_cpu.so (build container)
-  python tests/golden/make_golden.py gpu   # needs oracle/_ref/libfpref_gpu.so and a CUDA GPU
+  python tests/golden/make_golden.py gpu [OUT_DIR]  # needs oracle/_ref/libfpref_gpu.so and a CUDA GPU
+
+OUT_DIR (default: this folder) lets a run on a remote GPU machine write the
+file where that machine's results are collected; copy it here afterwards.
 
 The reference ships no golden vectors or known-answer tests, so these are
 outputs of the reference itself: its CPU functions (src/pipeline_utils.cpp,
@@ -68,7 +71,7 @@ def make_cpu() -> Path:
     return out
 
 
-def make_gpu() -> Path:
+def make_gpu(out_dir: Path = HERE) -> Path:
     from oracle_lib import Oracle, RefGpu
     from scene_util import hypotheses
 
@@ -92,7 +95,8 @@ def make_gpu() -> Path:
     scores[2] = scores.max() + 1.0
     scores[3] = scores[2]
     best_pose, best_score, best_idx = ref.select_best(moved, scores, s.center)
-    out = HERE / "ref_gpu.npz"
+    out_dir.mkdir(parents=True, exist_ok=True)
+    out = out_dir / "ref_gpu.npz"
     np.savez_compressed(
         out, rgb=s.rgb, depth=depth, mask=s.mask, k4=s.k4, verts=s.verts, normals=s.normals,
         colors=s.colors_u8, faces=s.faces, diameter=np.float32(s.diameter), center=s.center,
@@ -106,4 +110,7 @@ def make_gpu() -> Path:
 
 if __name__ == "__main__":
     which = sys.argv[1] if len(sys.argv) > 1 else "cpu"
-    print(make_cpu() if which == "cpu" else make_gpu())
+    if which == "cpu":
+        print(make_cpu())
+    else:
+        print(make_gpu(Path(sys.argv[2]) if len(sys.argv) > 2 else HERE))
