@@ -8,9 +8,10 @@
 //   warp 1     MMA issuer (one lane) + TMEM owner: tcgen05.mma kind::f16,
 //              M=128, N=BN, K=16, fp32 accumulators in TMEM, two accumulator
 //              buffers so the epilogue of tile i overlaps the MMAs of tile i+1.
-//   warps 2-5  epilogue: tcgen05.ld rows of the accumulator, bias / residual /
-//              positional embedding / ReLU, bf16|fp16 stores into the KP8
-//              destination layout chosen by the layer (see include/fpk.h).
+//   warps 2-9  epilogue, two warps per TMEM lane quarter (each converts half
+//              of the BN columns): tcgen05.ld rows of the accumulator, bias /
+//              residual / positional embedding / ReLU, bf16|fp16 stores into
+//              the KP8 destination layout chosen by the layer (see include/fpk.h).
 // The activation window uses the no-swizzle K-major core-matrix layout
 // [plane][row][16 B]; shifting a convolution tap by one row is a 16-byte move of
 // the descriptor start address, so all taps read the same staged window.
@@ -37,17 +38,26 @@ int checkLaunch(const char* what);
 
 namespace gemm {
 
-constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, each takes half the columns
+constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;  // elements per weight stage (128 bytes of bf16/fp16)
+constexpr int kMaxASlots = 4;
+constexpr int kMaxBStages = 8;
+constexpr int kMaxStagesPerChunk = FPK_GEMM_MAX_TAPS;  // 64-channel chunks: one stage per tap
+constexpr size_t kSmemBytes = 220 * 1024;  // dynamic shared memory per CTA
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 struct Smem {
-  uint64_t a_full[2], a_empty[2];
-  uint64_t b_full[8], b_empty[8];
+  uint64_t a_full[kMaxASlots], a_empty[kMaxASlots];
+  uint64_t b_full[kMaxBStages], b_empty[kMaxBStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
+  uint32_t pad;
+  // Per stage within a channel chunk: the four K=16 steps' A descriptor start
+  // offsets (16-byte units, relative to the window slot), packed 2 x u16 per word.
+  uint2 a_off[kMaxStagesPerChunk];
 };
 
 __device__ __forceinline__ uint32_t smemU32(const void* p) {
@@ -189,6 +199,7 @@ struct Plan {
   int n_chunks;      // cin / cw
   int stages_per_chunk;
   int min_off, win_rows;
+  int a_slots;       // activation windows in flight (2..kMaxASlots)
   int b_stages;
   int m_tiles, n_tiles;
   uint32_t a_win_bytes;  // per slot
@@ -256,19 +267,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* b_smem = base;
   unsigned char* a_smem = b_smem + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes;
-  Smem* sm = reinterpret_cast<Smem*>(a_smem + 2 * static_cast<size_t>(pl.a_win_bytes));
+  Smem* sm = reinterpret_cast<Smem*>(a_smem + static_cast<size_t>(pl.a_slots) * pl.a_win_bytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = d.error_flag;
   constexpr uint32_t kTmemCols = 2 * BN;
 
+  if (threadIdx.x < pl.stages_per_chunk * 2) {
+    // Descriptor start offsets of the two K=16 steps handled by this thread.
+    const uint32_t plane_units = static_cast<uint32_t>(pl.win_rows);  // plane bytes / 16
+    uint32_t packed = 0;
+    for (int h = 0; h < 2; ++h) {
+      const int k_local = threadIdx.x * 32 + h * 16;
+      const int tap = k_local / pl.cw;
+      const int c = k_local - tap * pl.cw;
+      const uint32_t off =
+          static_cast<uint32_t>(d.tap_off[tap] - pl.min_off) + static_cast<uint32_t>(c >> 3) * plane_units;
+      packed |= (off & 0xFFFFu) << (16 * h);
+    }
+    reinterpret_cast<uint32_t*>(sm->a_off)[threadIdx.x] = packed;
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
+      mbarInit(&sm->acc_full[i], 1);
+      mbarInit(&sm->acc_empty[i], kEpilogueWarps);
+    }
+    for (int i = 0; i < pl.a_slots; ++i) {
       mbarInit(&sm->a_full[i], 1);
       mbarInit(&sm->a_empty[i], 1);
-      mbarInit(&sm->acc_full[i], 1);
-      mbarInit(&sm->acc_empty[i], 4);
     }
     for (int i = 0; i < pl.b_stages; ++i) {
       mbarInit(&sm->b_full[i], 1);
@@ -293,39 +320,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- producer ----------------
       const unsigned char* a_bytes = static_cast<const unsigned char*>(d.a);
+      const uint32_t plane_bytes = static_cast<uint32_t>(pl.win_rows) * 16u;
       uint32_t a_iter = 0, b_iter = 0;
+      int slot = 0, bs = 0;
+      uint32_t a_phase = 0, b_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
         const int m0 = (tile / pl.n_tiles) * kBlockM;
         const int n0 = (tile % pl.n_tiles) * BN;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          const int slot = a_iter & 1;
-          ok = waitBar(&sm->a_empty[slot], ((a_iter >> 1) & 1) ^ 1, err, 11);
+          ok = waitBar(&sm->a_empty[slot], a_phase ^ 1, err, 11);
           if (!ok) break;
           mbarExpectTx(&sm->a_full[slot], pl.a_win_bytes);
           unsigned char* win = a_smem + static_cast<size_t>(slot) * pl.a_win_bytes;
-          const uint32_t plane_bytes = static_cast<uint32_t>(pl.win_rows) * 16u;
+          const unsigned char* src = a_bytes + static_cast<long long>(ch * pl.planes) * d.a_plane_stride +
+                                     static_cast<long long>(m0 + pl.min_off) * 16;
           for (int p = 0; p < pl.planes; ++p) {
-            const unsigned char* src = a_bytes +
-                                       static_cast<long long>(ch * pl.planes + p) * d.a_plane_stride +
-                                       static_cast<long long>(m0 + pl.min_off) * 16;
             bulkCopy(win + p * plane_bytes, src, plane_bytes, &sm->a_full[slot]);
+            src += d.a_plane_stride;
           }
           ++a_iter;
+          if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
-            const int bs = b_iter % pl.b_stages;
-            ok = waitBar(&sm->b_empty[bs], ((b_iter / pl.b_stages) & 1) ^ 1, err, 12);
+            ok = waitBar(&sm->b_empty[bs], b_phase ^ 1, err, 12);
             if (!ok) break;
             mbarExpectTx(&sm->b_full[bs], pl.b_stage_bytes);
             tmaLoad2d(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
                       ch * taps_cw + st * kBlockK, n0, &sm->b_full[bs]);
             ++b_iter;
+            if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
         }
       }
       // Drain: every load armed above must land before the CTA may exit.
-      for (uint32_t i = a_iter > 2 ? a_iter - 2 : 0; i < a_iter; ++i) {
-        drainBar(&sm->a_full[i & 1], (i >> 1) & 1);
+      const uint32_t na = static_cast<uint32_t>(pl.a_slots);
+      for (uint32_t i = a_iter > na ? a_iter - na : 0; i < a_iter; ++i) {
+        drainBar(&sm->a_full[i % na], (i / na) & 1);
       }
       const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
       for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
@@ -335,44 +365,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = instrDesc(BN, sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value);
-      uint32_t a_iter = 0, b_iter = 0, t_iter = 0;
+      // Descriptors are built once; per K=16 step only the 14-bit start
+      // address field changes (an add that cannot carry: every start is a
+      // valid shared-memory address below 2^18 bytes).
+      const uint32_t idesc = instrDesc(BN, std::is_same<T, __nv_bfloat16>::value);
+      const uint64_t a_desc0 =
+          smemDesc(smemU32(a_smem), static_cast<uint32_t>(pl.win_rows) * 16u, 128u, kLayoutNone);
+      const uint64_t b_desc0 = smemDesc(smemU32(b_smem), 16u, 1024u, kLayoutSw128);
+      const uint32_t a_slot_units = pl.a_win_bytes >> 4;
+      const uint32_t b_stage_units = pl.b_stage_bytes >> 4;
+      int slot = 0, bs = 0;
+      uint32_t a_phase = 0, b_phase = 0, t_iter = 0;
       bool ok = true;
-      const uint32_t a_plane_bytes = static_cast<uint32_t>(pl.win_rows) * 16u;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++t_iter) {
         const int buf = t_iter & 1;
         ok = waitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 13);
         if (!ok) break;
         tcFenceAfter();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
+        uint32_t accumulate = 0;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          const int slot = a_iter & 1;
-          ok = waitBar(&sm->a_full[slot], (a_iter >> 1) & 1, err, 14);
+          ok = waitBar(&sm->a_full[slot], a_phase, err, 14);
           if (!ok) break;
           tcFenceAfter();
-          const uint32_t win = smemU32(a_smem + static_cast<size_t>(slot) * pl.a_win_bytes);
+          const uint64_t a_base = a_desc0 + static_cast<uint64_t>(slot) * a_slot_units;
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
-            const int bs = b_iter % pl.b_stages;
-            ok = waitBar(&sm->b_full[bs], (b_iter / pl.b_stages) & 1, err, 15);
+            ok = waitBar(&sm->b_full[bs], b_phase, err, 15);
             if (!ok) break;
             tcFenceAfter();
-            const uint32_t bst = smemU32(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes);
-#pragma unroll
-            for (int ks = 0; ks < kBlockK / 16; ++ks) {
-              const int k_local = st * kBlockK + ks * 16;
-              const int tap = k_local / pl.cw;
-              const int c = k_local - tap * pl.cw;
-              const uint32_t a_addr = win + static_cast<uint32_t>(d.tap_off[tap] - pl.min_off) * 16u +
-                                      static_cast<uint32_t>(c >> 3) * a_plane_bytes;
-              const uint64_t a_desc = smemDesc(a_addr, a_plane_bytes, 128u, kLayoutNone);
-              const uint64_t b_desc = smemDesc(bst + ks * 32u, 16u, 1024u, kLayoutSw128);
-              tcMma(d_tmem, a_desc, b_desc, idesc, (ch | st | ks) != 0 ? 1u : 0u);
-            }
+            const uint2 offs = sm->a_off[st];
+            const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
+            tcMma(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+            tcMma(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
+            tcMma(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+            tcMma(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+            accumulate = 1u;
             tcCommit(&sm->b_empty[bs]);
-            ++b_iter;
+            if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
           tcCommit(&sm->a_empty[slot]);
-          ++a_iter;
+          if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
         }
         tcCommit(&sm->acc_full[buf]);
       }
@@ -381,8 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       waitBar(&sm->drain, 0, err, 16);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int col_half = (warp - 2) >> 2;    // which half of the BN columns
+    constexpr int kHalf = BN / 2;
     const int row_in_tile = quarter * 32 + lane;
     const unsigned char* res = static_cast<const unsigned char*>(d.residual);
     unsigned char* dst = static_cast<unsigned char*>(d.dst);
@@ -422,12 +456,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             drow = r;
         }
       }
+      const bool has_res = valid && res != nullptr;
+      const int j0 = col_half * kHalf;
+      // Residual rows of the next 32 columns are fetched while the current
+      // 32 are converted and stored.
+      uint4 rv[4] = {}, rn[4] = {};
+      if (has_res) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          rv[g] = *reinterpret_cast<const uint4*>(
+              res + static_cast<long long>((n0 + j0 + g * 8) >> 3) * d.res_plane_stride +
+              static_cast<long long>(r) * 16);
+        }
+      }
       const uint32_t t_base =
           tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
 #pragma unroll 1
-      for (int j = 0; j < BN; j += 32) {
+      for (int j = j0; j < j0 + kHalf; j += 32) {
         uint32_t acc[32];
         FPB_TMEM_LD32(t_base + j, acc);
+        if (has_res && j + 32 < j0 + kHalf) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            rn[g] = *reinterpret_cast<const uint4*>(
+                res + static_cast<long long>((n0 + j + 32 + g * 8) >> 3) * d.res_plane_stride +
+                static_cast<long long>(r) * 16);
+          }
+        }
         tmemWaitLd();
         if (valid) {
 #pragma unroll
@@ -442,14 +497,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
               v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
             }
-            if (res != nullptr) {
-              float rv[8];
-              unpack8<T>(*reinterpret_cast<const uint4*>(res + static_cast<long long>(n >> 3) *
-                                                                   d.res_plane_stride +
-                                                               static_cast<long long>(r) * 16),
-                         rv);
+            if (has_res) {
+              float rf[8];
+              unpack8<T>(rv[g], rf);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] += rv[e];
+              for (int e = 0; e < 8; ++e) v[e] += rf[e];
             }
             if (d.relu) {
 #pragma unroll
@@ -465,6 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       drow * 16) = pack8<T>(v);
           }
         }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) rv[g] = rn[g];
       }
       tcFenceBefore();
       __syncwarp();
@@ -539,7 +593,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   if (dev < 31 && !(attr_mask & (1 << dev))) {
     const cudaError_t e = cudaFuncSetAttribute(gemmKernel<T, BN>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(220 * 1024));
+                                               static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) {
       cudaGetLastError();
       return fail(std::string("fpk_gemm smem attribute: ") + cudaGetErrorString(e));
@@ -580,6 +634,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   pl.n_chunks = d.cin / pl.cw;
   if ((d.taps * pl.cw) % kBlockK != 0) return fail("fpk_gemm: taps*chunk must be a multiple of 64");
   pl.stages_per_chunk = d.taps * pl.cw / kBlockK;
+  if (pl.stages_per_chunk > kMaxStagesPerChunk) return fail("fpk_gemm: too many weight stages per chunk");
   int mn = d.tap_off[0], mx = d.tap_off[0];
   for (int t = 1; t < d.taps; ++t) {
     mn = d.tap_off[t] < mn ? d.tap_off[t] : mn;
@@ -593,15 +648,22 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     return fail("fpk_gemm: cout must be 64, 128 or a multiple of 256");
   }
   pl.b_stage_bytes = static_cast<uint32_t>(bn) * 128u;
-  const size_t budget = 220 * 1024 - 1024 - sizeof(Smem) - 2 * static_cast<size_t>(pl.a_win_bytes);
-  int stages = static_cast<int>(budget / pl.b_stage_bytes);
-  if (stages > 8) stages = 8;
+  // Few weight stages per channel chunk (1x1 layers) need more activation
+  // windows in flight; convolutions reuse one window for all taps.
+  int stages = 0;
+  for (int slots = pl.stages_per_chunk >= 4 ? 2 : kMaxASlots; slots >= 2; --slots) {
+    const size_t used = 1024 + sizeof(Smem) + static_cast<size_t>(slots) * pl.a_win_bytes;
+    stages = used < kSmemBytes ? static_cast<int>((kSmemBytes - used) / pl.b_stage_bytes) : 0;
+    pl.a_slots = slots;
+    if (stages >= 4 || slots == 2) break;
+  }
+  if (stages > kMaxBStages) stages = kMaxBStages;
   if (stages < 2) return fail("fpk_gemm: activation window too large for shared memory");
   pl.b_stages = stages;
   pl.m_tiles = (d.rows + kBlockM - 1) / kBlockM;
   pl.n_tiles = d.cout / bn;
   const size_t smem = 1024 + static_cast<size_t>(stages) * pl.b_stage_bytes +
-                      2 * static_cast<size_t>(pl.a_win_bytes) + sizeof(Smem);
+                      static_cast<size_t>(pl.a_slots) * pl.a_win_bytes + sizeof(Smem);
   const int kprime = pl.n_chunks * d.taps * pl.cw;
   CUtensorMap map;
   if (makeWeightMap(d, kprime, bn, &map) != 0) return 1;
