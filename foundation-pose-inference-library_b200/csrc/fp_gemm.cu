@@ -1,6 +1,7 @@
 // Persistent tcgen05 implicit-GEMM kernel (sm_100a) for RefineNet / ScoreNet.
 //
-// One CTA per SM walks output tiles of 128 rows x BN channels. Warp roles:
+// One CTA per SM walks output tiles of 128 (or, for layers of at most 128
+// output channels, 256) rows x BN channels. Warp roles:
 //   warp 0     producer: per 64-channel chunk, one bulk copy per channel plane
 //              brings a window of 128 + span rows of the activation into shared
 //              memory (reused by every tap of the convolution); per 64-wide K
@@ -9,7 +10,8 @@
 //              M=128, N=BN, K=16, fp32 accumulators in TMEM, two accumulator
 //              buffers so the epilogue of tile i overlaps the MMAs of tile i+1.
 //   warps 2-9  epilogue, two warps per TMEM lane quarter (each converts half
-//              of the BN columns): tcgen05.ld rows of the accumulator, bias /
+//              of the BN columns, or with 256-row tiles one 128-row half):
+//              tcgen05.ld rows of the accumulator, bias /
 //              residual / positional embedding / ReLU, bf16|fp16 stores into
 //              the KP8 destination layout chosen by the layer (see include/fpk.h).
 // The activation window uses the no-swizzle K-major core-matrix layout
@@ -258,7 +260,10 @@ __device__ __forceinline__ void unpack8<__half>(uint4 u, float* v) {
   }
 }
 
-template <typename T, int BN>
+// MH = output row halves per tile: 1 -> 128 x BN tiles; 2 -> 256 x BN tiles
+// whose two 128-row halves share every weight stage (two MMAs per K step into
+// separate accumulators), halving weight traffic for the narrow layers.
+template <typename T, int BN, int MH>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -272,7 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = d.error_flag;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kTmemCols = 2 * MH * BN;
+  constexpr int kTileM = kBlockM * MH;
+  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 
   if (threadIdx.x < pl.stages_per_chunk * 2) {
     // Descriptor start offsets of the two K=16 steps handled by this thread.
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t a_phase = 0, b_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
-        const int m0 = (tile / pl.n_tiles) * kBlockM;
+        const int m0 = (tile / pl.n_tiles) * kTileM;
         const int n0 = (tile % pl.n_tiles) * BN;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
           ok = waitBar(&sm->a_empty[slot], a_phase ^ 1, err, 11);
@@ -382,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = waitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 13);
         if (!ok) break;
         tcFenceAfter();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * MH * BN);
         uint32_t accumulate = 0;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
           ok = waitBar(&sm->a_full[slot], a_phase, err, 14);
@@ -395,10 +402,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tcFenceAfter();
             const uint2 offs = sm->a_off[st];
             const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
-            tcMma(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-            tcMma(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
-            tcMma(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-            tcMma(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {
+              // Half h reads the window 128 rows (128 x 16 B = 128 units) further on.
+              const uint64_t ah = a_base + static_cast<uint64_t>(h * 128);
+              const uint32_t dh = d_tmem + static_cast<uint32_t>(h * BN);
+              tcMma(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              tcMma(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
+              tcMma(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              tcMma(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
+            }
             accumulate = 1u;
             tcCommit(&sm->b_empty[bs]);
             if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
@@ -414,15 +427,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
-    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int col_half = (warp - 2) >> 2;    // which half of the BN columns
-    constexpr int kHalf = BN / 2;
-    const int row_in_tile = quarter * 32 + lane;
+    const int quarter = warp & 3;    // TMEM lane quarter this warp may access
+    const int pair = (warp - 2) >> 2;  // MH=1: half of the BN columns; MH=2: row half
+    constexpr int kSpan = MH == 1 ? BN / 2 : BN;  // columns converted by one warp
+    const int m_half = MH == 1 ? 0 : pair;
+    const int row_in_tile = m_half * kBlockM + quarter * 32 + lane;
     const unsigned char* res = static_cast<const unsigned char*>(d.residual);
     unsigned char* dst = static_cast<unsigned char*>(d.dst);
     uint32_t t_iter = 0;
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t_iter) {
-      const int m0 = (tile / pl.n_tiles) * kBlockM;
+      const int m0 = (tile / pl.n_tiles) * kTileM;
       const int n0 = (tile % pl.n_tiles) * BN;
       const int buf = t_iter & 1;
       if (!waitBar(&sm->acc_full[buf], (t_iter >> 1) & 1, err, 17)) break;
@@ -457,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const bool has_res = valid && res != nullptr;
-      const int j0 = col_half * kHalf;
+      const int j0 = MH == 1 ? pair * kSpan : 0;
       // Residual rows of the next 32 columns are fetched while the current
       // 32 are converted and stored.
       uint4 rv[4] = {}, rn[4] = {};
@@ -470,12 +484,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const uint32_t t_base =
-          tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+          tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+          static_cast<uint32_t>((buf * MH + m_half) * BN);
 #pragma unroll 1
-      for (int j = j0; j < j0 + kHalf; j += 32) {
+      for (int j = j0; j < j0 + kSpan; j += 32) {
         uint32_t acc[32];
         FPB_TMEM_LD32(t_base + j, acc);
-        if (has_res && j + 32 < j0 + kHalf) {
+        if (has_res && j + 32 < j0 + kSpan) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             rn[g] = *reinterpret_cast<const uint4*>(
@@ -584,14 +599,14 @@ int numSms() {
   return value;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, int MH>
 int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, size_t smem,
            cudaStream_t stream) {
   static int attr_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 31 && !(attr_mask & (1 << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(gemmKernel<T, BN>,
+    const cudaError_t e = cudaFuncSetAttribute(gemmKernel<T, BN, MH>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) {
@@ -603,7 +618,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   const int tiles = pl.m_tiles * pl.n_tiles;
   const int grid = tiles < numSms() ? tiles : numSms();
   prof::countLaunch(prof::kGemm);
-  gemmKernel<T, BN><<<grid, kThreads, smem, stream>>>(d, pl, map);
+  gemmKernel<T, BN, MH><<<grid, kThreads, smem, stream>>>(d, pl, map);
   return checkLaunch("gemmKernel");
 }
 
@@ -640,41 +655,55 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     mn = d.tap_off[t] < mn ? d.tap_off[t] : mn;
     mx = d.tap_off[t] > mx ? d.tap_off[t] : mx;
   }
-  pl.min_off = mn;
-  pl.win_rows = kBlockM + (mx - mn);
-  pl.a_win_bytes = static_cast<uint32_t>(pl.planes * pl.win_rows * 16);
   int bn = d.cout >= 256 ? 256 : d.cout;
   if (d.cout % bn != 0 || (bn != 64 && bn != 128 && bn != 256)) {
     return fail("fpk_gemm: cout must be 64, 128 or a multiple of 256");
   }
+  pl.min_off = mn;
   pl.b_stage_bytes = static_cast<uint32_t>(bn) * 128u;
-  // Few weight stages per channel chunk (1x1 layers) need more activation
-  // windows in flight; convolutions reuse one window for all taps.
-  int stages = 0;
-  for (int slots = pl.stages_per_chunk >= 4 ? 2 : kMaxASlots; slots >= 2; --slots) {
-    const size_t used = 1024 + sizeof(Smem) + static_cast<size_t>(slots) * pl.a_win_bytes;
-    stages = used < kSmemBytes ? static_cast<int>((kSmemBytes - used) / pl.b_stage_bytes) : 0;
-    pl.a_slots = slots;
-    if (stages >= 4 || slots == 2) break;
+  // Shared-memory plan for tiles of 128 * mh rows: activation window slots
+  // (1x1 layers, with few weight stages per chunk, want more of them in
+  // flight; convolutions reuse one window for all taps) and weight stages.
+  auto plan = [&](int mh) {
+    pl.win_rows = kBlockM * mh + (mx - mn);
+    pl.a_win_bytes = static_cast<uint32_t>(pl.planes * pl.win_rows * 16);
+    int stages = 0;
+    for (int slots = pl.stages_per_chunk >= 4 ? 2 : kMaxASlots; slots >= 2; --slots) {
+      const size_t used = 1024 + sizeof(Smem) + static_cast<size_t>(slots) * pl.a_win_bytes;
+      stages = used < kSmemBytes ? static_cast<int>((kSmemBytes - used) / pl.b_stage_bytes) : 0;
+      pl.a_slots = slots;
+      if (stages >= 4 || slots == 2) break;
+    }
+    pl.b_stages = stages > kMaxBStages ? kMaxBStages : stages;
+    pl.m_tiles = (d.rows + kBlockM * mh - 1) / (kBlockM * mh);
+    pl.n_tiles = d.cout / bn;
+    return pl.b_stages >= 2;
+  };
+  // Narrow layers (BN <= 128) take 256-row tiles when there are enough rows
+  // to keep every SM busy.
+  int mh = 1;
+  if (bn <= 128 && (d.rows + kBlockM - 1) / kBlockM >= 2 * numSms() && plan(2)) {
+    mh = 2;
+  } else if (!plan(1)) {
+    return fail("fpk_gemm: activation window too large for shared memory");
   }
-  if (stages > kMaxBStages) stages = kMaxBStages;
-  if (stages < 2) return fail("fpk_gemm: activation window too large for shared memory");
-  pl.b_stages = stages;
-  pl.m_tiles = (d.rows + kBlockM - 1) / kBlockM;
-  pl.n_tiles = d.cout / bn;
-  const size_t smem = 1024 + static_cast<size_t>(stages) * pl.b_stage_bytes +
+  const size_t smem = 1024 + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes +
                       static_cast<size_t>(pl.a_slots) * pl.a_win_bytes + sizeof(Smem);
   const int kprime = pl.n_chunks * d.taps * pl.cw;
   CUtensorMap map;
   if (makeWeightMap(d, kprime, bn, &map) != 0) return 1;
   auto s = static_cast<cudaStream_t>(stream);
   const bool bf = d.dtype == FPK_DTYPE_BF16;
+  if (mh == 2) {
+    if (bn == 64) return bf ? launch<__nv_bfloat16, 64, 2>(d, pl, map, smem, s) : launch<__half, 64, 2>(d, pl, map, smem, s);
+    return bf ? launch<__nv_bfloat16, 128, 2>(d, pl, map, smem, s) : launch<__half, 128, 2>(d, pl, map, smem, s);
+  }
   switch (bn) {
     case 64:
-      return bf ? launch<__nv_bfloat16, 64>(d, pl, map, smem, s) : launch<__half, 64>(d, pl, map, smem, s);
+      return bf ? launch<__nv_bfloat16, 64, 1>(d, pl, map, smem, s) : launch<__half, 64, 1>(d, pl, map, smem, s);
     case 128:
-      return bf ? launch<__nv_bfloat16, 128>(d, pl, map, smem, s) : launch<__half, 128>(d, pl, map, smem, s);
+      return bf ? launch<__nv_bfloat16, 128, 1>(d, pl, map, smem, s) : launch<__half, 128, 1>(d, pl, map, smem, s);
     default:
-      return bf ? launch<__nv_bfloat16, 256>(d, pl, map, smem, s) : launch<__half, 256>(d, pl, map, smem, s);
+      return bf ? launch<__nv_bfloat16, 256, 1>(d, pl, map, smem, s) : launch<__half, 256, 1>(d, pl, map, smem, s);
   }
 }

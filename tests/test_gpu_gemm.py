@@ -85,14 +85,19 @@ def test_plain_gemm(fpk, err, m, cin, cout, dtype):
     assert torch.count_nonzero(out.t[:, :256]) == 0
 
 
-@pytest.mark.parametrize("cin,cout,hw,dtype", [(64, 128, 20, FPK_DTYPE_BF16),
-                                               (128, 128, 40, FPK_DTYPE_F16),
-                                               (256, 256, 40, FPK_DTYPE_BF16),
-                                               (512, 512, 20, FPK_DTYPE_BF16)])
-def test_conv3x3_residual_relu(fpk, err, cin, cout, hw, dtype):
-    g = torch.Generator().manual_seed(cin * 7 + hw)
+# n=24 images of 40x40 give more than 2 x 148 tiles of 128 rows, which
+# selects the 256-row tiles (two accumulators per weight stage) for the
+# layers of at most 128 output channels.
+@pytest.mark.parametrize("cin,cout,hw,dtype,n", [(64, 128, 20, FPK_DTYPE_BF16, 3),
+                                                 (128, 128, 40, FPK_DTYPE_F16, 3),
+                                                 (128, 128, 40, FPK_DTYPE_F16, 24),
+                                                 (64, 64, 40, FPK_DTYPE_BF16, 24),
+                                                 (256, 256, 40, FPK_DTYPE_BF16, 3),
+                                                 (512, 512, 20, FPK_DTYPE_BF16, 3)])
+def test_conv3x3_residual_relu(fpk, err, cin, cout, hw, dtype, n):
+    g = torch.Generator().manual_seed(cin * 7 + hw + n)
     dt = DT[dtype]
-    n, H, W = 3, hw, hw
+    H, W = hw, hw
     gw = W + 1
     img_rows = (H + 1) * gw
     rows = n * img_rows
@@ -177,13 +182,13 @@ def test_s2d_stride2_conv(fpk, err, dtype):
     close(got, ref.permute(0, 2, 3, 1))
 
 
-@pytest.mark.parametrize("dtype", [FPK_DTYPE_BF16])
-def test_stem_7x7_stride2(fpk, err, dtype):
+@pytest.mark.parametrize("dtype,n", [(FPK_DTYPE_BF16, 2), (FPK_DTYPE_F16, 8)])
+def test_stem_7x7_stride2(fpk, err, dtype, n):
     """7x7 stride-2 pad-3 conv over 6 channels as a 16-tap conv on the 32-channel
     space-to-depth layout the fused render+pack writes (grid 83 for 160 crops)."""
     g = torch.Generator().manual_seed(9)
     dt = DT[dtype]
-    n, S, cin, cout = 2, 160, 6, 64
+    S, cin, cout = 160, 6, 64
     gs = (S + 7) // 2  # 83
     X = torch.randn(n, cin, S, S, generator=g)
     Wt = torch.randn(cout, cin, 7, 7, generator=g) / math.sqrt(49 * cin)
