@@ -20,6 +20,7 @@ struct AttnArgs {
   int seq_len;
   int heads;
   float scale_log2;  // log2(e) / sqrt(head_dim)
+  int* error_flag;   // device flag set by the tensor-core kernel on a timed-out wait
 };
 
 struct LnArgs {
@@ -34,6 +35,8 @@ struct LnArgs {
 };
 
 cudaError_t launchAttention(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s);
+// tcgen05 / TMEM attention (fp_attention.cu); same arguments, needs error_flag.
+cudaError_t launchAttentionTc(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s);
 cudaError_t launchLayerNorm(const LnArgs& a, bool bf16, cudaStream_t s);
 cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int seq_len, int n_seq,
                             float* out, bool bf16, cudaStream_t s);

@@ -471,9 +471,10 @@ void NetworkRunner::refine(int count, int first_chunk, float* delta_t, float* de
   at.seq_len = kTokens;
   at.heads = 4;
   at.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
+  at.error_flag = err_;
   {
     prof::Scope scope(prof::kAttention, 2.0 * 4 * count * 4.0 * kTokens * kTokens * 128, s);
-    check(net::launchAttention(at, 2, count, bf, s), "attention");
+    check(net::launchAttentionTc(at, 2, count, bf, s), "attention");
   }
   float* outs[2] = {delta_t, delta_r};
   const char* heads[2] = {"trans", "rot"};
@@ -515,9 +516,10 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
   at.seq_len = kTokens;
   at.heads = 4;
   at.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
+  at.error_flag = err_;
   {
     prof::Scope scope(prof::kAttention, 1.0 * 4 * n * 4.0 * kTokens * kTokens * 128, s);
-    check(net::launchAttention(at, 1, n, bf, s), "attention");
+    check(net::launchAttentionTc(at, 1, n, bf, s), "attention");
   }
   gemm(net.L("out_proj"), a.att, 0, T, a.y1, FPK_DST_SAME, t, 1, t, 1, false, nullptr, 0, 0, 1, 0, nullptr, s);
   check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, n, a.feat, bf, s), "token mean");
