@@ -10,17 +10,20 @@
 //              straight into the no-swizzle core-matrix layout
 //              [plane][row][16 B] the tensor core reads.
 //   warp 1     MMA issuer (one lane) + TMEM owner:
-//                S_b = Q K_b^T   (M=128, N=64, K=128; A, B K-major)  -> TMEM
-//                O  += P_b V_b   (M=128, N=128, K=64; V MN-major)     -> TMEM
+//                S_b = Q K_b^T   (M=128, N=64, K=128; A, B K-major)   -> TMEM
+//                O  += P_b V_b   (M=128, N=128, K=64; A = P from TMEM,
+//                                 B = V MN-major from shared memory)  -> TMEM
 //              S is double-buffered so S_{b+1} runs while block b is in the
-//              softmax.
-//   warps 2-5  softmax, one query row per thread: tcgen05.ld of S, running
-//              max / sum in the log2 domain, P = 2^(s - m) as fp16/bf16 into
-//              shared memory (the A operand of the PV product). O is rescaled
-//              in TMEM only when a row's maximum grows by more than 8 (a
-//              factor of 256), which keeps P below 256 and the result exact;
-//              at the end O / l is written back to KP8.
-// Shared memory 112 KB and 256 TMEM columns per CTA, so two CTAs share an SM
+//              softmax; a buffer is reused once the PV product that read its
+//              P has completed.
+//   warps 2-5  softmax, one query row per thread: one tcgen05.ld of the row's
+//              64 scores, running max / sum in the log2 domain, P = 2^(s - m)
+//              packed as fp16/bf16 pairs and stored (tcgen05.st) over the first
+//              32 columns of the same S buffer. O is rescaled in TMEM only when
+//              a row's maximum grows by more than 8 (a factor of 256), which
+//              keeps P below 256 and the result exact; at the end O / l is
+//              written back to KP8.
+// Shared memory 96 KB and 256 TMEM columns per CTA, so two CTAs share an SM
 // and overlap each other's loads, softmax and MMAs. All mbarrier waits are
 // bounded (fp_tc.cuh) and report through AttnArgs::error_flag.
 #include <cuda_bf16.h>
@@ -43,7 +46,6 @@ constexpr int kKeys = 64;                  // keys per block
 constexpr int kPlanes = 16;                // 128 head channels / 8
 constexpr uint32_t kQBytes = kPlanes * kRows * 16;   // 32 KB
 constexpr uint32_t kKVBytes = kPlanes * kKeys * 16;  // 16 KB
-constexpr uint32_t kPBytes = (kKeys / 8) * kRows * 16;  // 16 KB
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 256;        // S[2] (2 x 64) + O (128)
 constexpr uint32_t kOCol = 2 * kKeys;
@@ -54,17 +56,24 @@ struct Bars {
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2];
-  uint64_t p_full, p_free;
+  uint64_t p_full, p_free;  // P_b in TMEM ready / PV_b complete
   uint64_t o_done;
   uint32_t tmem_base;
 };
 
-constexpr size_t kSmemBytes = 128 + kQBytes + 4 * kKVBytes + kPBytes + sizeof(Bars);
+constexpr size_t kSmemBytes = 128 + kQBytes + 4 * kKVBytes + sizeof(Bars);
 
 __host__ __device__ constexpr uint32_t idescF16(int n, bool bf16, bool b_mn_major) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(kRows >> 4) << 24);
+}
+
+// 2^x with the MUFU ex2 instruction (flush-to-zero, ~2 ulp); 2^-inf = 0.
+__device__ __forceinline__ float exp2Approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 template <typename T>
@@ -88,8 +97,7 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
   unsigned char* q_s = base;
   unsigned char* k_s = q_s + kQBytes;           // [2][16 planes][64 keys][16 B]
   unsigned char* v_s = k_s + 2 * kKVBytes;      // [2][16 planes][64 keys][16 B]
-  unsigned char* p_s = v_s + 2 * kKVBytes;      // [8 key planes][128 rows][16 B]
-  Bars* bars = reinterpret_cast<Bars*>(p_s + kPBytes);
+  Bars* bars = reinterpret_cast<Bars*>(v_s + 2 * kKVBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -112,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
       mbarInit(&bars->v_full[i], 1);
       mbarInit(&bars->v_empty[i], 1);
       mbarInit(&bars->s_full[i], 1);
-      mbarInit(&bars->s_free[i], 4);
+      mbarInit(&bars->s_free[i], 1);
     }
     mbarInit(&bars->p_full, 4);
     mbarInit(&bars->p_free, 1);
@@ -185,7 +193,6 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
       const uint32_t q_addr = smemU32(q_s);
       const uint32_t k_addr = smemU32(k_s);
       const uint32_t v_addr = smemU32(v_s);
-      const uint32_t p_addr = smemU32(p_s);
       bool ok = waitBar(&bars->q_full, 0, err, 23);
       tcFenceAfter();
       for (int b = 0; b <= n_blocks && ok; ++b) {
@@ -220,16 +227,17 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
           const int keys = min(kKeys, a.seq_len - j * kKeys);
           const int steps = (keys + 15) >> 4;
           for (int ks = 0; ks < steps; ++ks) {
-            // P: K-major A, 16 keys = two key planes per step. V: MN-major B,
-            // 8-key core matrices 128 B apart (LBO), 8-channel planes kKeys*16
-            // bytes apart (SBO).
-            const uint64_t ad = smemDesc(p_addr + ks * 2 * (kRows * 16), kRows * 16, 128, kLayoutNone);
+            // P: A operand in TMEM, 16 keys = 8 columns of packed pairs. V:
+            // MN-major B, 8-key core matrices 128 B apart (LBO), 8-channel
+            // planes kKeys*16 bytes apart (SBO).
+            const uint32_t at = tmem + static_cast<uint32_t>(slot * kKeys + ks * 8);
             const uint64_t bd = smemDesc(v_addr + slot * kKVBytes + ks * 16 * 16, 128, kKeys * 16,
                                          kLayoutNone);
-            tcMma(tmem + kOCol, ad, bd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
+            tcMmaTmemA(tmem + kOCol, at, bd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
           }
           tcCommit(&bars->p_free);
           tcCommit(&bars->v_empty[slot]);
+          tcCommit(&bars->s_free[slot]);
         }
       }
       tcCommit(&bars->o_done);
@@ -247,33 +255,34 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
       ok = waitBar(&bars->s_full[slot], (b >> 1) & 1, err, 28);
       if (!ok) break;
       tcFenceAfter();
-      const int key0 = b * kKeys;
-      const int keys = min(kKeys, a.seq_len - key0);
-      // Pass 1: block maximum (log2 domain).
-      float mb = -INFINITY;
+      const int keys = min(kKeys, a.seq_len - b * kKeys);
+      // One TMEM read of the row's 64 scores (two 32-column loads, one wait).
+      uint32_t sv[kKeys];
+      FPB_TMEM_LD32(lane_base + slot * kKeys, sv);
+      FPB_TMEM_LD32(lane_base + slot * kKeys + 32, (sv + 32));
+      tmemWaitLd();
+      if (keys < kKeys) {
+        // Last block: keys past the sequence contribute nothing.
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 32) {
-        uint32_t sv[32];
-        FPB_TMEM_LD32(lane_base + slot * kKeys + c, sv);
-        tmemWaitLd();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if (c + e < keys) mb = fmaxf(mb, __uint_as_float(sv[e]) * a.scale_log2);
+        for (int e = 0; e < kKeys; ++e) {
+          if (e >= keys) sv[e] = __float_as_uint(-INFINITY);
         }
       }
-      // PV of block b-1 must be complete before P is overwritten or O rescaled.
-      if (b >= 1) {
-        ok = waitBar(&bars->p_free, (b - 1) & 1, err, 29);
-        if (!ok) break;
-        tcFenceAfter();
-      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kKeys; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      const float mb = mx * a.scale_log2;  // scale_log2 > 0 commutes with max
       const float m_new = fmaxf(m, mb);
       if (b == 0) {
         m = m_new;
       } else {
         const bool grow = m_new > m + kRescaleLog2;
         if (__any_sync(0xffffffffu, grow)) {
-          const float f = grow ? exp2f(m - m_new) : 1.0f;
+          // O holds blocks < b once PV_{b-1} has completed.
+          ok = waitBar(&bars->p_free, (b - 1) & 1, err, 29);
+          if (!ok) break;
+          tcFenceAfter();
+          const float f = grow ? exp2Approx(m - m_new) : 1.0f;
 #pragma unroll 1
           for (int c = 0; c < 128; c += 32) {
             uint32_t ov[32];
@@ -290,36 +299,22 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
           }
         }
       }
-      // Pass 2: P = 2^(s - m) into the PV operand, running sum.
+      // P = 2^(s * scale - m) (masked keys give 2^-inf = 0), packed in pairs
+      // over the first 32 columns of this S buffer: the PV product's A operand.
+      const float neg_m = -m;
+      uint32_t pk[kKeys / 2];
 #pragma unroll
-      for (int c = 0; c < kKeys; c += 32) {
-        uint32_t sv[32];
-        FPB_TMEM_LD32(lane_base + slot * kKeys + c, sv);
-        tmemWaitLd();
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          float pv[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int k = c + g * 8 + e;
-            pv[e] = k < keys ? exp2f(__uint_as_float(sv[g * 8 + e]) * a.scale_log2 - m) : 0.0f;
-            l += pv[e];
-          }
-          uint4 w;
-          w.x = pack2<T>(pv[0], pv[1]);
-          w.y = pack2<T>(pv[2], pv[3]);
-          w.z = pack2<T>(pv[4], pv[5]);
-          w.w = pack2<T>(pv[6], pv[7]);
-          *reinterpret_cast<uint4*>(p_s + ((c >> 3) + g) * (kRows * 16) + r * 16) = w;
-        }
+      for (int e = 0; e < kKeys; e += 2) {
+        const float p0 = exp2Approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, neg_m));
+        const float p1 = exp2Approx(fmaf(__uint_as_float(sv[e + 1]), a.scale_log2, neg_m));
+        l += p0 + p1;
+        pk[e >> 1] = pack2<T>(p0, p1);
       }
-      fenceProxyAsyncSmem();
+      FPB_TMEM_ST32(lane_base + slot * kKeys, pk);
+      tmemStoreWait();
       tcFenceBefore();
       __syncwarp();
-      if (lane == 0) {
-        mbarArrive(&bars->s_free[slot]);
-        mbarArrive(&bars->p_full);
-      }
+      if (lane == 0) mbarArrive(&bars->p_full);
     }
     if (ok) ok = waitBar(&bars->o_done, 0, err, 30);
     if (ok) {

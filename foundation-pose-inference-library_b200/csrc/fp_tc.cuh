@@ -111,6 +111,18 @@ __device__ __forceinline__ void tcMma(uint32_t d_tmem, uint64_t a_desc, uint64_t
       : "memory");
 }
 
+// D (TMEM) (+)= A (TMEM, K-major, 16-bit elements packed in pairs per
+// 32-bit column) x B (shared memory descriptor).
+__device__ __forceinline__ void tcMmaTmemA(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 #define FPB_TMEM_LD32(taddr, r)                                                                  \
   asm volatile(                                                                                  \
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "    \
