@@ -517,8 +517,10 @@ __device__ __forceinline__ void shadePixel(const RenderArgs& a, const HypState& 
 }
 
 // reference src/cuda_pipeline.cu:370-407 sampleRgbBilinear.
+// lut255[v] holds v / 255.0f (filled with that division on the device, so
+// the table lookup returns the reference's quotient bit for bit).
 __device__ __forceinline__ float3 sampleRgbBilinear(const uint8_t* rgb, int width, int height,
-                                                    float x, float y) {
+                                                    float x, float y, const float* lut255) {
   if (x < 0.0f || y < 0.0f || x > static_cast<float>(width - 1) ||
       y > static_cast<float>(height - 1)) {
     return make_float3(0.0f, 0.0f, 0.0f);
@@ -533,18 +535,18 @@ __device__ __forceinline__ float3 sampleRgbBilinear(const uint8_t* rgb, int widt
   const uint8_t* q10 = rgb + (y0 * width + x1) * 3;
   const uint8_t* q01 = rgb + (y1 * width + x0) * 3;
   const uint8_t* q11 = rgb + (y1 * width + x1) * 3;
-  const float3 c00 = make_float3(static_cast<float>(__ldg(q00 + 0)) / 255.0f,
-                                 static_cast<float>(__ldg(q00 + 1)) / 255.0f,
-                                 static_cast<float>(__ldg(q00 + 2)) / 255.0f);
-  const float3 c10 = make_float3(static_cast<float>(__ldg(q10 + 0)) / 255.0f,
-                                 static_cast<float>(__ldg(q10 + 1)) / 255.0f,
-                                 static_cast<float>(__ldg(q10 + 2)) / 255.0f);
-  const float3 c01 = make_float3(static_cast<float>(__ldg(q01 + 0)) / 255.0f,
-                                 static_cast<float>(__ldg(q01 + 1)) / 255.0f,
-                                 static_cast<float>(__ldg(q01 + 2)) / 255.0f);
-  const float3 c11 = make_float3(static_cast<float>(__ldg(q11 + 0)) / 255.0f,
-                                 static_cast<float>(__ldg(q11 + 1)) / 255.0f,
-                                 static_cast<float>(__ldg(q11 + 2)) / 255.0f);
+  const float3 c00 = make_float3(lut255[__ldg(q00 + 0)],
+                                 lut255[__ldg(q00 + 1)],
+                                 lut255[__ldg(q00 + 2)]);
+  const float3 c10 = make_float3(lut255[__ldg(q10 + 0)],
+                                 lut255[__ldg(q10 + 1)],
+                                 lut255[__ldg(q10 + 2)]);
+  const float3 c01 = make_float3(lut255[__ldg(q01 + 0)],
+                                 lut255[__ldg(q01 + 1)],
+                                 lut255[__ldg(q01 + 2)]);
+  const float3 c11 = make_float3(lut255[__ldg(q11 + 0)],
+                                 lut255[__ldg(q11 + 1)],
+                                 lut255[__ldg(q11 + 2)]);
   return make_float3((1.0f - ty) * ((1.0f - tx) * c00.x + tx * c10.x) +
                          ty * ((1.0f - tx) * c01.x + tx * c11.x),
                      (1.0f - ty) * ((1.0f - tx) * c00.y + tx * c10.y) +
@@ -580,7 +582,8 @@ struct PackedPixel {
 
 __device__ __forceinline__ PackedPixel packPixel(const RenderArgs& a, const HypState& hs, int x,
                                                  int y, int crop_width, int crop_height,
-                                                 float3 rend_rgb, float3 rend_xyz) {
+                                                 float3 rend_rgb, float3 rend_xyz,
+                                                 const float* lut255) {
   const float4 box = hs.box;
   const float crop_w = fmaxf(box.z - box.x, 1.0f);
   const float crop_h = fmaxf(box.w - box.y, 1.0f);
@@ -594,7 +597,7 @@ __device__ __forceinline__ PackedPixel packPixel(const RenderArgs& a, const HypS
   }
   const float3 t = make_float3(hs.pose[3], hs.pose[7], hs.pose[11]);
   const float radius = fmaxf(a.diameter * 0.5f, 1e-6f);
-  const float3 obs_rgb = sampleRgbBilinear(a.frame_rgb, a.img_w, a.img_h, src_x, src_y);
+  const float3 obs_rgb = sampleRgbBilinear(a.frame_rgb, a.img_w, a.img_h, src_x, src_y, lut255);
   float3 obs_xyz = observedXyz(a.frame_depth, a.img_w, a.img_h, a.k, a.p, src_x, src_y);
   const bool obs_invalid = obs_xyz.z < a.invalid_threshold;
   obs_xyz = make_float3((obs_xyz.x - t.x) / radius, (obs_xyz.y - t.y) / radius,
@@ -679,7 +682,9 @@ __global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) 
   int* big_list = reinterpret_cast<int*>(smem_raw + static_cast<size_t>(a.rows_per_band) * width * 8);
   __shared__ HypState hs;
   __shared__ int big_count;
+  __shared__ float lut255[256];
   const int tid = threadIdx.x;
+  if (tid < 256) lut255[tid] = static_cast<float>(tid) / 255.0f;
 
   if (tid < 12) {
     hs.pose[tid] = a.poses[hyp * 16 + tid];
@@ -717,14 +722,27 @@ __global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) 
         continue;
       }
     }
-    for (int py = y_lo; py <= y_hi; ++py) {
-      const float fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
-      const float p0y = rowTerm(fy, s.p0);
-      const float p1y = rowTerm(fy, s.p1);
-      const float p2y = rowTerm(fy, s.p2);
-      unsigned long long* zrow = zbuf + (py - row0) * width;
-      for (int px = s.min_x; px <= s.max_x; ++px) {
-        rasterPixel(s, px, inv_w, p0y, p1y, p2y, tri + 1, zrow);
+    // One flat loop over the bounding box (row terms refreshed on each new
+    // row): a warp runs as many iterations as its largest box, instead of
+    // its tallest box times its widest row.
+    const int npx = (s.max_x - s.min_x + 1) * (y_hi - y_lo + 1);
+    int px = s.min_x;
+    int py = y_lo;
+    float fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
+    float p0y = rowTerm(fy, s.p0);
+    float p1y = rowTerm(fy, s.p1);
+    float p2y = rowTerm(fy, s.p2);
+    unsigned long long* zrow = zbuf + (py - row0) * width;
+    for (int i = 0; i < npx; ++i) {
+      rasterPixel(s, px, inv_w, p0y, p1y, p2y, tri + 1, zrow);
+      if (++px > s.max_x) {
+        px = s.min_x;
+        ++py;
+        fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
+        p0y = rowTerm(fy, s.p0);
+        p1y = rowTerm(fy, s.p1);
+        p2y = rowTerm(fy, s.p2);
+        zrow += width;
       }
     }
   }
@@ -772,7 +790,7 @@ __global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) 
         a.tri_ids[(static_cast<size_t>(hyp) * height + py) * width + px] = tri_plus_one;
       }
     } else {
-      const PackedPixel pk = packPixel(a, hs, px, y, width, height, rgb, xyz);
+      const PackedPixel pk = packPixel(a, hs, px, y, width, height, rgb, xyz, lut255);
       using T = typename std::conditional<
           kOut == RenderOut::kS2dF32, float,
           typename std::conditional<kOut == RenderOut::kS2dF16, __half, __nv_bfloat16>::type>::type;
@@ -790,6 +808,9 @@ __global__ void packNchwKernel(RenderArgs a, const float* __restrict__ rend_rgb,
   const int height = a.p.input_height;
   const long long total = static_cast<long long>(a.n) * width * height;
   const long long linear = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  __shared__ float lut255[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut255[i] = static_cast<float>(i) / 255.0f;
+  __syncthreads();
   if (linear >= total) {
     return;
   }
@@ -802,7 +823,7 @@ __global__ void packNchwKernel(RenderArgs a, const float* __restrict__ rend_rgb,
   const size_t o = (static_cast<size_t>(s) * height + y) * width + x;
   const float3 rgb = make_float3(rend_rgb[3 * o], rend_rgb[3 * o + 1], rend_rgb[3 * o + 2]);
   const float3 xyz = make_float3(rend_xyz[3 * o], rend_xyz[3 * o + 1], rend_xyz[3 * o + 2]);
-  const PackedPixel pk = packPixel(a, hs, x, y, width, height, rgb, xyz);
+  const PackedPixel pk = packPixel(a, hs, x, y, width, height, rgb, xyz, lut255);
   const size_t plane = static_cast<size_t>(width) * height;
   for (int c = 0; c < 6; ++c) {
     net_r[(static_cast<size_t>(s) * 6 + c) * plane + static_cast<size_t>(y) * width + x] = pk.r[c];
@@ -975,9 +996,18 @@ int maxDynamicSmem() {
     cudaGetDevice(&dev);
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, renderKernel<RenderOut::kNhwc>);
-    value = optin - static_cast<int>(fa.sharedSizeBytes) - 256;
+    // The output variants differ in static shared memory (only the packing
+    // ones hold the 1/255 table): budget for the largest.
+    size_t stat = 0;
+    const void* kernels[4] = {reinterpret_cast<const void*>(renderKernel<RenderOut::kNhwc>),
+                              reinterpret_cast<const void*>(renderKernel<RenderOut::kS2dF32>),
+                              reinterpret_cast<const void*>(renderKernel<RenderOut::kS2dF16>),
+                              reinterpret_cast<const void*>(renderKernel<RenderOut::kS2dBf16>)};
+    for (const void* k : kernels) {
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, k) == cudaSuccess && fa.sharedSizeBytes > stat) stat = fa.sharedSizeBytes;
+    }
+    value = optin - static_cast<int>(stat) - 256;
   }
   return value;
 }
