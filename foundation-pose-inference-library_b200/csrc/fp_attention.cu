@@ -23,18 +23,23 @@
 //              a row's maximum grows by more than 8 (a factor of 256), which
 //              keeps P below 256 and the result exact; at the end O / l is
 //              written back to KP8.
-// Shared memory 96 KB and 256 TMEM columns per CTA, so two CTAs share an SM
-// and overlap each other's loads, softmax and MMAs. All mbarrier waits are
+// fp16/bf16 run kind::f16 with 96 KB of shared memory and 256 TMEM columns
+// per CTA, so two CTAs share an SM and overlap each other's loads, softmax and
+// MMAs; fp32 activations run kind::tf32 (TF32 math) with 192 KB, one CTA. All mbarrier waits are
 // bounded (fp_tc.cuh) and report through AttnArgs::error_flag.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
+#include <string>
 #include <type_traits>
 
 #include "fp_net_kernels.cuh"
+#include "fp_profile.hpp"
 #include "fp_tc.cuh"
+#include "fpk.h"
 
 namespace fpb {
 namespace attn {
@@ -43,10 +48,33 @@ using namespace fpb::tc;
 
 constexpr int kRows = 128;                 // query rows per tile = TMEM lanes
 constexpr int kKeys = 64;                  // keys per block
-constexpr int kPlanes = 16;                // 128 head channels / 8
-constexpr uint32_t kQBytes = kPlanes * kRows * 16;   // 32 KB
-constexpr uint32_t kKVBytes = kPlanes * kKeys * 16;  // 16 KB
-constexpr int kThreads = 192;
+constexpr int kHeadDim = 128;
+
+// Per element type: 16-byte records hold 8 (fp16/bf16) or 4 (fp32) channels;
+// every MMA K step reads 32 bytes (two records) of each row: K=16 under
+// kind::f16, K=8 under kind::tf32.
+template <typename T>
+struct Geo {
+  static constexpr bool kTf32 = std::is_same<T, float>::value;
+  static constexpr int kPerRecord = 16 / static_cast<int>(sizeof(T));
+  static constexpr int kPlanes = kHeadDim / kPerRecord;            // 16 or 32
+  static constexpr uint32_t kQBytes = kPlanes * kRows * 16;        // 32 or 64 KB
+  static constexpr uint32_t kKVBytes = kPlanes * kKeys * 16;       // 16 or 32 KB
+  static constexpr int kStepKeys = 32 / static_cast<int>(sizeof(T));  // keys per PV K step
+  // TF32 takes MN-major operands only in the 32-byte-atom 128B swizzle, so
+  // fp32 V blocks are transposed in shared memory by two extra warps into a
+  // K-major [4-key plane][channel][16 B] tile, from a staging copy whose
+  // planes are padded by 16 bytes (conflict-free column reads). P is kept in
+  // shared memory too, as a K-major [4-key plane][row][16 B] tile.
+  static constexpr int kThreads = kTf32 ? 256 : 192;
+  static constexpr uint32_t kVRawPlane = kKeys * 16 + (kTf32 ? 16 : 0);
+  static constexpr uint32_t kVBytes = kTf32 ? kPlanes * kVRawPlane : 2 * kKVBytes;
+  static constexpr uint32_t kVTBytes = kTf32 ? kKVBytes : 0;
+  static constexpr uint32_t kPBytes = kTf32 ? (kKeys / kPerRecord) * kRows * 16 : 0;
+  static constexpr size_t kSmem = 128 + kQBytes + 2 * kKVBytes + kVBytes + kVTBytes + kPBytes + 256;
+  static constexpr int kMinBlocks = kTf32 ? 1 : 2;
+  static constexpr uint32_t fmt() { return kTf32 ? 2u : (std::is_same<T, __nv_bfloat16>::value ? 1u : 0u); }
+};
 constexpr uint32_t kTmemCols = 256;        // S[2] (2 x 64) + O (128)
 constexpr uint32_t kOCol = 2 * kKeys;
 constexpr float kRescaleLog2 = 8.0f;
@@ -56,17 +84,44 @@ struct Bars {
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2];
-  uint64_t p_full, p_free;  // P_b in TMEM ready / PV_b complete
+  uint64_t p_full, p_free;  // P_b ready / PV_b complete
+  uint64_t vt_full, vt_empty;  // fp32: transposed V tile ready / consumed
   uint64_t o_done;
   uint32_t tmem_base;
 };
 
-constexpr size_t kSmemBytes = 128 + kQBytes + 4 * kKVBytes + sizeof(Bars);
+static_assert(sizeof(Bars) <= 256, "barrier block");
 
-__host__ __device__ constexpr uint32_t idescF16(int n, bool bf16, bool b_mn_major) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
-         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(kRows >> 4) << 24);
+// Instruction descriptor: fp32 accumulate, A K-major, B K- or MN-major.
+__host__ __device__ constexpr uint32_t idesc(uint32_t fmt, int n, bool b_mn_major) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
+}
+
+template <typename T>
+__device__ __forceinline__ void mmaSS(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  if constexpr (Geo<T>::kTf32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+  } else {
+    tcMma(d, a, b, id, acc);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void mmaTS(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  if constexpr (Geo<T>::kTf32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
+        : "memory");
+  } else {
+    tcMmaTmemA(d, a_tmem, b, id, acc);
+  }
 }
 
 // 2^x with the MUFU ex2 instruction (flush-to-zero, ~2 ulp); 2^-inf = 0.
@@ -90,14 +145,20 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::AttnArgs a) {
+__global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentionTcKernel(const net::AttnArgs a) {
+  using G = Geo<T>;
+  constexpr int kPlanes = G::kPlanes;
+  constexpr uint32_t kQBytes = G::kQBytes;
+  constexpr uint32_t kKVBytes = G::kKVBytes;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
   unsigned char* q_s = base;
-  unsigned char* k_s = q_s + kQBytes;           // [2][16 planes][64 keys][16 B]
-  unsigned char* v_s = k_s + 2 * kKVBytes;      // [2][16 planes][64 keys][16 B]
-  Bars* bars = reinterpret_cast<Bars*>(v_s + 2 * kKVBytes);
+  unsigned char* k_s = q_s + kQBytes;           // [2][planes][64 keys][16 B]
+  unsigned char* v_s = k_s + 2 * kKVBytes;      // [2][planes][64 keys][16 B]; fp32: padded staging
+  unsigned char* vt_s = v_s + G::kVBytes;       // fp32 only: [16 key planes][128 ch][16 B]
+  unsigned char* p_s = vt_s + G::kVTBytes;      // fp32 only: [16 key planes][128 rows][16 B]
+  Bars* bars = reinterpret_cast<Bars*>(p_s + G::kPBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -118,13 +179,15 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
       mbarInit(&bars->k_full[i], 1);
       mbarInit(&bars->k_empty[i], 1);
       mbarInit(&bars->v_full[i], 1);
-      mbarInit(&bars->v_empty[i], 1);
+      mbarInit(&bars->v_empty[i], G::kTf32 ? 2 : 1);
       mbarInit(&bars->s_full[i], 1);
       mbarInit(&bars->s_free[i], 1);
     }
     mbarInit(&bars->p_full, 4);
     mbarInit(&bars->p_free, 1);
     mbarInit(&bars->o_done, 1);
+    mbarInit(&bars->vt_full, 2);
+    mbarInit(&bars->vt_empty, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -165,16 +228,21 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
                    a.qkv + static_cast<long long>(kp + p) * a.qkv_plane_stride + r0 * 16,
                    kKeys * 16, &bars->k_full[slot]);
         }
-        if (b >= 2) ok = waitBar(&bars->v_empty[slot], ((b >> 1) - 1) & 1, err, 22);
+        // V: double-buffered (16-bit), or one staging buffer (fp32) that the
+        // transpose warps release.
+        const int vslot = G::kTf32 ? 0 : slot;
+        if (G::kTf32 ? b >= 1 : b >= 2) {
+          ok = waitBar(&bars->v_empty[vslot], G::kTf32 ? ((b - 1) & 1) : (((b >> 1) - 1) & 1), err, 22);
+        }
         if (!ok) {
           issued = 2 * b + 1;
           break;
         }
-        mbarExpectTx(&bars->v_full[slot], kKVBytes);
+        mbarExpectTx(&bars->v_full[vslot], kKVBytes);
         for (int p = 0; p < kPlanes; ++p) {
-          bulkCopy(v_s + slot * kKVBytes + p * (kKeys * 16),
+          bulkCopy(v_s + (G::kTf32 ? p * G::kVRawPlane : slot * kKVBytes + p * (kKeys * 16)),
                    a.qkv + static_cast<long long>(vp + p) * a.qkv_plane_stride + r0 * 16,
-                   kKeys * 16, &bars->v_full[slot]);
+                   kKeys * 16, &bars->v_full[vslot]);
         }
         issued = 2 * b + 2;
       }
@@ -182,14 +250,18 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
       drainBar(&bars->q_full, 0);
       for (int i = issued > 4 ? issued - 4 : 0; i < issued; ++i) {
         const int b = i >> 1;
-        drainBar((i & 1) ? &bars->v_full[b & 1] : &bars->k_full[b & 1], (b >> 1) & 1);
+        if ((i & 1) && G::kTf32) {
+          drainBar(&bars->v_full[0], b & 1);
+        } else {
+          drainBar((i & 1) ? &bars->v_full[b & 1] : &bars->k_full[b & 1], (b >> 1) & 1);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      const uint32_t idesc_o = idescF16(128, kBf16, true);
+      // PV: V as an MN-major B operand (16-bit), or the transposed K-major tile (fp32).
+      const uint32_t idesc_o = idesc(G::fmt(), kHeadDim, !G::kTf32);
       const uint32_t q_addr = smemU32(q_s);
       const uint32_t k_addr = smemU32(k_s);
       const uint32_t v_addr = smemU32(v_s);
@@ -204,15 +276,15 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
           tcFenceAfter();
           const int keys = min(kKeys, a.seq_len - b * kKeys);
           const int n = (keys + 15) & ~15;
-          const uint32_t idesc_s = idescF16(n, kBf16, false);
+          const uint32_t idesc_s = idesc(G::fmt(), n, false);
           const uint32_t d = tmem + static_cast<uint32_t>(slot * kKeys);
 #pragma unroll
           for (int ks = 0; ks < kPlanes / 2; ++ks) {
-            // 16 head channels = two planes per K step.
+            // 32 bytes of head channels = two planes per K step.
             const uint64_t ad = smemDesc(q_addr + ks * 2 * (kRows * 16), kRows * 16, 128, kLayoutNone);
             const uint64_t bd = smemDesc(k_addr + slot * kKVBytes + ks * 2 * (kKeys * 16), kKeys * 16,
                                          128, kLayoutNone);
-            tcMma(d, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+            mmaSS<T>(d, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
           }
           tcCommit(&bars->s_full[slot]);
           tcCommit(&bars->k_empty[slot]);
@@ -221,29 +293,40 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
           const int j = b - 1;
           const int slot = j & 1;
           ok = waitBar(&bars->p_full, j & 1, err, 26);
-          if (ok) ok = waitBar(&bars->v_full[slot], (j >> 1) & 1, err, 27);
+          if (ok) {
+            ok = G::kTf32 ? waitBar(&bars->vt_full, j & 1, err, 27)
+                          : waitBar(&bars->v_full[slot], (j >> 1) & 1, err, 27);
+          }
           if (!ok) break;
           tcFenceAfter();
           const int keys = min(kKeys, a.seq_len - j * kKeys);
-          const int steps = (keys + 15) >> 4;
+          const int steps = (keys + G::kStepKeys - 1) / G::kStepKeys;
           for (int ks = 0; ks < steps; ++ks) {
-            // P: A operand in TMEM, 16 keys = 8 columns of packed pairs. V:
-            // MN-major B, 8-key core matrices 128 B apart (LBO), 8-channel
-            // planes kKeys*16 bytes apart (SBO).
-            const uint32_t at = tmem + static_cast<uint32_t>(slot * kKeys + ks * 8);
-            const uint64_t bd = smemDesc(v_addr + slot * kKVBytes + ks * 16 * 16, 128, kKeys * 16,
-                                         kLayoutNone);
-            tcMmaTmemA(tmem + kOCol, at, bd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
+            // P: A operand in TMEM, one K step = 8 columns (16 keys packed in
+            // pairs, or 8 fp32 keys). V: MN-major B, 8-key core matrices 128 B
+            // apart (LBO), channel planes kKeys*16 bytes apart (SBO).
+            if constexpr (G::kTf32) {
+              // 8 keys = two 4-key planes per K step, for P (A) and V^T (B).
+              const uint64_t ad = smemDesc(smemU32(p_s) + ks * 2 * (kRows * 16), kRows * 16, 128, kLayoutNone);
+              const uint64_t bd = smemDesc(smemU32(vt_s) + ks * 2 * (kHeadDim * 16), kHeadDim * 16, 128,
+                                           kLayoutNone);
+              mmaSS<T>(tmem + kOCol, ad, bd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
+            } else {
+              const uint64_t bd = smemDesc(v_addr + slot * kKVBytes + ks * G::kStepKeys * 16, 128,
+                                           kKeys * 16, kLayoutNone);
+              const uint32_t at = tmem + static_cast<uint32_t>(slot * kKeys + ks * 8);
+              mmaTS<T>(tmem + kOCol, at, bd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
+            }
           }
           tcCommit(&bars->p_free);
-          tcCommit(&bars->v_empty[slot]);
+          tcCommit(G::kTf32 ? &bars->vt_empty : &bars->v_empty[slot]);
           tcCommit(&bars->s_free[slot]);
         }
       }
       tcCommit(&bars->o_done);
       drainBar(&bars->o_done, 0);
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------- softmax + output (warps 2..5) ----------------
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -299,18 +382,39 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
           }
         }
       }
-      // P = 2^(s * scale - m) (masked keys give 2^-inf = 0), packed in pairs
-      // over the first 32 columns of this S buffer: the PV product's A operand.
+      // P = 2^(s * scale - m) (masked keys give 2^-inf = 0) over this S
+      // buffer: the PV product's A operand (16-bit pairs in the first 32
+      // columns, or fp32 in place).
       const float neg_m = -m;
-      uint32_t pk[kKeys / 2];
+      if constexpr (G::kTf32) {
+        // The single P buffer is free once PV_{b-1} has completed.
+        if (b >= 1) {
+          ok = waitBar(&bars->p_free, (b - 1) & 1, err, 31);
+          if (!ok) break;
+        }
 #pragma unroll
-      for (int e = 0; e < kKeys; e += 2) {
-        const float p0 = exp2Approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, neg_m));
-        const float p1 = exp2Approx(fmaf(__uint_as_float(sv[e + 1]), a.scale_log2, neg_m));
-        l += p0 + p1;
-        pk[e >> 1] = pack2<T>(p0, p1);
+        for (int e = 0; e < kKeys; e += 4) {
+          float4 w;
+          w.x = exp2Approx(fmaf(__uint_as_float(sv[e + 0]), a.scale_log2, neg_m));
+          w.y = exp2Approx(fmaf(__uint_as_float(sv[e + 1]), a.scale_log2, neg_m));
+          w.z = exp2Approx(fmaf(__uint_as_float(sv[e + 2]), a.scale_log2, neg_m));
+          w.w = exp2Approx(fmaf(__uint_as_float(sv[e + 3]), a.scale_log2, neg_m));
+          l += (w.x + w.y) + (w.z + w.w);
+          *reinterpret_cast<float4*>(p_s + (e >> 2) * (kRows * 16) + r * 16) =
+              make_float4(tf32Round(w.x), tf32Round(w.y), tf32Round(w.z), tf32Round(w.w));
+        }
+        fenceProxyAsyncSmem();
+      } else {
+        uint32_t pk[kKeys / 2];
+#pragma unroll
+        for (int e = 0; e < kKeys; e += 2) {
+          const float p0 = exp2Approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, neg_m));
+          const float p1 = exp2Approx(fmaf(__uint_as_float(sv[e + 1]), a.scale_log2, neg_m));
+          l += p0 + p1;
+          pk[e >> 1] = pack2<T>(p0, p1);
+        }
+        FPB_TMEM_ST32(lane_base + slot * kKeys, pk);
       }
-      FPB_TMEM_ST32(lane_base + slot * kKeys, pk);
       tmemStoreWait();
       tcFenceBefore();
       __syncwarp();
@@ -329,19 +433,54 @@ __global__ void __launch_bounds__(kThreads, 2) attentionTcKernel(const net::Attn
         FPB_TMEM_LD32(lane_base + kOCol + c, ov);
         tmemWaitLd();
         if (store) {
+          if constexpr (G::kTf32) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 w;
-            w.x = pack2<T>(__uint_as_float(ov[g * 8 + 0]) * inv, __uint_as_float(ov[g * 8 + 1]) * inv);
-            w.y = pack2<T>(__uint_as_float(ov[g * 8 + 2]) * inv, __uint_as_float(ov[g * 8 + 3]) * inv);
-            w.z = pack2<T>(__uint_as_float(ov[g * 8 + 4]) * inv, __uint_as_float(ov[g * 8 + 5]) * inv);
-            w.w = pack2<T>(__uint_as_float(ov[g * 8 + 6]) * inv, __uint_as_float(ov[g * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(out + static_cast<long long>(op + (c >> 3) + g) * a.out_plane_stride) = w;
+            for (int g = 0; g < 8; ++g) {
+              const float4 w = make_float4(tf32Round(__uint_as_float(ov[g * 4 + 0]) * inv),
+                                           tf32Round(__uint_as_float(ov[g * 4 + 1]) * inv),
+                                           tf32Round(__uint_as_float(ov[g * 4 + 2]) * inv),
+                                           tf32Round(__uint_as_float(ov[g * 4 + 3]) * inv));
+              *reinterpret_cast<float4*>(out + static_cast<long long>(op + (c >> 2) + g) * a.out_plane_stride) = w;
+            }
+          } else {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 w;
+              w.x = pack2<T>(__uint_as_float(ov[g * 8 + 0]) * inv, __uint_as_float(ov[g * 8 + 1]) * inv);
+              w.y = pack2<T>(__uint_as_float(ov[g * 8 + 2]) * inv, __uint_as_float(ov[g * 8 + 3]) * inv);
+              w.z = pack2<T>(__uint_as_float(ov[g * 8 + 4]) * inv, __uint_as_float(ov[g * 8 + 5]) * inv);
+              w.w = pack2<T>(__uint_as_float(ov[g * 8 + 6]) * inv, __uint_as_float(ov[g * 8 + 7]) * inv);
+              *reinterpret_cast<uint4*>(out + static_cast<long long>(op + (c >> 3) + g) * a.out_plane_stride) = w;
+            }
           }
         }
       }
     }
     tcFenceBefore();
+  } else if constexpr (G::kTf32) {
+    // ---------------- V transpose (fp32 only, warps 6..7) ----------------
+    // staging [ch plane][key][4 ch] -> V^T [key plane][ch][4 keys].
+    const int t = threadIdx.x - 192;  // 0..63
+    bool ok = true;
+    for (int b = 0; b < n_blocks && ok; ++b) {
+      ok = waitBar(&bars->v_full[0], b & 1, err, 32);
+      if (ok && b >= 1) ok = waitBar(&bars->vt_empty, (b - 1) & 1, err, 33);
+      if (!ok) break;
+      tcFenceAfter();
+      for (int rec = t; rec < (kKeys / 4) * kHeadDim; rec += 64) {
+        const int kp = rec / kHeadDim;
+        const int ch = rec - kp * kHeadDim;
+        const float* src = reinterpret_cast<const float*>(v_s + (ch >> 2) * G::kVRawPlane + kp * 64) + (ch & 3);
+        *reinterpret_cast<float4*>(vt_s + kp * (kHeadDim * 16) + ch * 16) =
+            make_float4(src[0], src[4], src[8], src[12]);
+      }
+      fenceProxyAsyncSmem();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) {
+        mbarArrive(&bars->v_empty[0]);
+        mbarArrive(&bars->vt_full);
+      }
+    }
   }
   __syncthreads();
   if (warp == 1) {
@@ -358,12 +497,13 @@ cudaError_t launch(const net::AttnArgs& a, int layers, int n_seq, cudaStream_t s
   if (dev < 31 && !(attr_mask & (1 << dev))) {
     const cudaError_t e = cudaFuncSetAttribute(attentionTcKernel<T>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kSmemBytes));
+                                               static_cast<int>(Geo<T>::kSmem));
     if (e != cudaSuccess) return e;
     attr_mask |= 1 << dev;
   }
   const int q_tiles = (a.seq_len + kRows - 1) / kRows;
-  attentionTcKernel<T><<<dim3(q_tiles, layers * a.heads, n_seq), kThreads, kSmemBytes, s>>>(a);
+  prof::countLaunch(prof::kAttention);
+  attentionTcKernel<T><<<dim3(q_tiles, layers * a.heads, n_seq), Geo<T>::kThreads, Geo<T>::kSmem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -371,10 +511,58 @@ cudaError_t launch(const net::AttnArgs& a, int layers, int n_seq, cudaStream_t s
 
 namespace net {
 
-cudaError_t launchAttentionTc(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s) {
+cudaError_t launchAttentionTc(const AttnArgs& a, int layers, int n_seq, int dtype, cudaStream_t s) {
   if (a.seq_len <= 0 || a.error_flag == nullptr) return cudaErrorInvalidValue;
-  return bf16 ? attn::launch<__nv_bfloat16>(a, layers, n_seq, s) : attn::launch<__half>(a, layers, n_seq, s);
+  switch (dtype) {
+    case FPK_DTYPE_BF16:
+      return attn::launch<__nv_bfloat16>(a, layers, n_seq, s);
+    case FPK_DTYPE_F32:
+      return attn::launch<float>(a, layers, n_seq, s);
+    default:
+      return attn::launch<__half>(a, layers, n_seq, s);
+  }
 }
 
 }  // namespace net
 }  // namespace fpb
+
+namespace fpb {
+int fail(const std::string& msg);
+int checkLaunch(const char* what);
+}  // namespace fpb
+
+extern "C" int fpk_attention(const void* qkv, long long qkv_plane_stride, int qkv_layer_channels,
+                             int q_channel, int k_channel, int v_channel, void* out,
+                             long long out_plane_stride, int out_layer_channels, int layers, int heads,
+                             int seq_len, int n_seq, int dtype, int* error_flag, void* stream) {
+  if (qkv == nullptr || out == nullptr || error_flag == nullptr) return fpb::fail("fpk_attention: null pointer");
+  if (dtype != FPK_DTYPE_F16 && dtype != FPK_DTYPE_BF16 && dtype != FPK_DTYPE_F32) {
+    return fpb::fail("fpk_attention: dtype must be f16, bf16 or f32");
+  }
+  const int per = dtype == FPK_DTYPE_F32 ? 4 : 8;
+  if (seq_len <= 0 || n_seq <= 0 || layers <= 0 || heads <= 0 || qkv_layer_channels % per ||
+      q_channel % per || k_channel % per || v_channel % per || out_layer_channels % per) {
+    return fpb::fail("fpk_attention: bad sizes");
+  }
+  if (reinterpret_cast<uintptr_t>(qkv) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
+      qkv_plane_stride % 16 || out_plane_stride % 16) {
+    return fpb::fail("fpk_attention: pointers and plane strides must be 16-byte aligned");
+  }
+  fpb::net::AttnArgs a{};
+  a.qkv = static_cast<const unsigned char*>(qkv);
+  a.qkv_plane_stride = qkv_plane_stride;
+  a.qkv_layer_planes = qkv_layer_channels / per;
+  a.q_plane = q_channel / per;
+  a.k_plane = k_channel / per;
+  a.v_plane = v_channel / per;
+  a.out = static_cast<unsigned char*>(out);
+  a.out_plane_stride = out_plane_stride;
+  a.out_layer_planes = out_layer_channels / per;
+  a.seq_len = seq_len;
+  a.heads = heads;
+  a.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
+  a.error_flag = error_flag;
+  const cudaError_t e = fpb::net::launchAttentionTc(a, layers, n_seq, dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fpb::fail(std::string("fpk_attention: ") + cudaGetErrorString(e));
+  return 0;
+}

@@ -46,7 +46,7 @@ using namespace fpb::tc;
 constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, each takes half the columns
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kBlockM = 128;
-constexpr int kBlockK = 64;  // elements per weight stage (128 bytes of bf16/fp16)
+constexpr int kStageBytes = 128;  // K bytes per weight stage: 64 fp16/bf16 or 32 fp32 elements
 constexpr int kMaxASlots = 4;
 constexpr int kMaxBStages = 8;
 constexpr int kMaxStagesPerChunk = FPK_GEMM_MAX_TAPS;  // 64-channel chunks: one stage per tap
@@ -64,10 +64,37 @@ struct Smem {
   uint2 a_off[kMaxStagesPerChunk];
 };
 
-// Instruction descriptor, kind::f16: fp32 accumulate, A/B K-major.
-__host__ __device__ constexpr uint32_t instrDesc(int bn, bool bf16) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
-         (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(kBlockM >> 4) << 24);
+// Element type traits. Every K step of the MMA reads 32 bytes of each row:
+// K=16 for fp16/bf16 (kind::f16), K=8 for fp32 read as TF32 (kind::tf32).
+// A 16-byte activation record holds 8 (16-bit) or 4 (fp32) channels.
+template <typename T>
+struct Elem {
+  static constexpr int kBytes = sizeof(T);
+  static constexpr int kPerRecord = 16 / kBytes;          // channels per 16-byte record
+  static constexpr int kPerStage = kStageBytes / kBytes;  // K elements per weight stage
+  static constexpr bool kTf32 = std::is_same<T, float>::value;
+  // Instruction descriptor: fp32 accumulate, A/B K-major, A/B format F16=0 /
+  // BF16=1 / TF32=2.
+  static constexpr uint32_t fmt() { return kTf32 ? 2u : (std::is_same<T, __nv_bfloat16>::value ? 1u : 0u); }
+  static constexpr uint32_t instrDesc(int bn, int m) {
+    return (1u << 4) | (fmt() << 7) | (fmt() << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void mmaT(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                     uint32_t accumulate) {
+  if constexpr (Elem<T>::kTf32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    tcMma(d_tmem, a_desc, b_desc, idesc, accumulate);
+  }
 }
 
 struct Plan {
@@ -135,6 +162,45 @@ __device__ __forceinline__ void unpack8<__half>(uint4 u, float* v) {
   }
 }
 
+// Eight consecutive channels starting at channel c (a multiple of 8) of row
+// `row` in a planar activation: one 16-byte record for 16-bit types, two
+// (channels c..c+3 and c+4..c+7 in consecutive planes) for fp32.
+template <typename T>
+__device__ __forceinline__ void loadRec8(const unsigned char* base, long long plane_stride, int c,
+                                         long long row, uint4* out) {
+  constexpr int kP = Elem<T>::kPerRecord;
+  const unsigned char* q = base + static_cast<long long>(c / kP) * plane_stride + row * 16;
+  out[0] = *reinterpret_cast<const uint4*>(q);
+  if constexpr (kP == 4) out[1] = *reinterpret_cast<const uint4*>(q + plane_stride);
+}
+
+template <typename T>
+__device__ __forceinline__ void unpackRec8(const uint4* in, float* v) {
+  if constexpr (Elem<T>::kTf32) {
+    const float4 a = *reinterpret_cast<const float4*>(&in[0]);
+    const float4 b = *reinterpret_cast<const float4*>(&in[1]);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    unpack8<T>(in[0], v);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void storeRec8(unsigned char* base, long long plane_stride, int c,
+                                          long long row, const float* v) {
+  constexpr int kP = Elem<T>::kPerRecord;
+  unsigned char* q = base + static_cast<long long>(c / kP) * plane_stride + row * 16;
+  if constexpr (Elem<T>::kTf32) {
+    // fp32 outputs are the next layer's TF32 operands: round to nearest here.
+    *reinterpret_cast<float4*>(q) = make_float4(tf32Round(v[0]), tf32Round(v[1]), tf32Round(v[2]), tf32Round(v[3]));
+    *reinterpret_cast<float4*>(q + plane_stride) =
+        make_float4(tf32Round(v[4]), tf32Round(v[5]), tf32Round(v[6]), tf32Round(v[7]));
+  } else {
+    *reinterpret_cast<uint4*>(q) = pack8<T>(v);
+  }
+}
+
 // MH = output row halves per tile: 1 -> 128 x BN tiles; 2 -> 256 x BN tiles
 // whose two 128-row halves share every weight stage (two MMAs per K step into
 // separate accumulators), halving weight traffic for the narrow layers.
@@ -157,15 +223,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 
   if (threadIdx.x < pl.stages_per_chunk * 2) {
-    // Descriptor start offsets of the two K=16 steps handled by this thread.
+    // Descriptor start offsets of the two 32-byte K steps handled by this thread.
+    constexpr int kStep = 32 / Elem<T>::kBytes;  // K elements per MMA
     const uint32_t plane_units = static_cast<uint32_t>(pl.win_rows);  // plane bytes / 16
     uint32_t packed = 0;
     for (int h = 0; h < 2; ++h) {
-      const int k_local = threadIdx.x * 32 + h * 16;
+      const int k_local = (threadIdx.x * 2 + h) * kStep;
       const int tap = k_local / pl.cw;
       const int c = k_local - tap * pl.cw;
-      const uint32_t off =
-          static_cast<uint32_t>(d.tap_off[tap] - pl.min_off) + static_cast<uint32_t>(c >> 3) * plane_units;
+      const uint32_t off = static_cast<uint32_t>(d.tap_off[tap] - pl.min_off) +
+                           static_cast<uint32_t>(c / Elem<T>::kPerRecord) * plane_units;
       packed |= (off & 0xFFFFu) << (16 * h);
     }
     reinterpret_cast<uint32_t*>(sm->a_off)[threadIdx.x] = packed;
@@ -228,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             mbarExpectTx(&sm->b_full[bs], pl.b_stage_bytes);
             tmaLoad2d(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
-                      ch * taps_cw + st * kBlockK, n0, &sm->b_full[bs]);
+                      ch * taps_cw + st * Elem<T>::kPerStage, n0, &sm->b_full[bs]);
             ++b_iter;
             if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
@@ -250,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Descriptors are built once; per K=16 step only the 14-bit start
       // address field changes (an add that cannot carry: every start is a
       // valid shared-memory address below 2^18 bytes).
-      const uint32_t idesc = instrDesc(BN, std::is_same<T, __nv_bfloat16>::value);
+      const uint32_t idesc = Elem<T>::instrDesc(BN, kBlockM);
       const uint64_t a_desc0 =
           smemDesc(smemU32(a_smem), static_cast<uint32_t>(pl.win_rows) * 16u, 128u, kLayoutNone);
       const uint64_t b_desc0 = smemDesc(smemU32(b_smem), 16u, 1024u, kLayoutSw128);
@@ -282,10 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               // Half h reads the window 128 rows (128 x 16 B = 128 units) further on.
               const uint64_t ah = a_base + static_cast<uint64_t>(h * 128);
               const uint32_t dh = d_tmem + static_cast<uint32_t>(h * BN);
-              tcMma(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-              tcMma(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
-              tcMma(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-              tcMma(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
+              mmaT<T>(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              mmaT<T>(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
+              mmaT<T>(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              mmaT<T>(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
             }
             accumulate = 1u;
             tcCommit(&sm->b_empty[bs]);
@@ -349,14 +416,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j0 = MH == 1 ? pair * kSpan : 0;
       // Residual rows of the next 32 columns are fetched while the current
       // 32 are converted and stored.
-      uint4 rv[4] = {}, rn[4] = {};
+      uint4 rv[4][2] = {}, rn[4][2] = {};
       if (has_res) {
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          rv[g] = *reinterpret_cast<const uint4*>(
-              res + static_cast<long long>((n0 + j0 + g * 8) >> 3) * d.res_plane_stride +
-              static_cast<long long>(r) * 16);
-        }
+        for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j0 + g * 8, r, rv[g]);
       }
       const uint32_t t_base =
           tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -367,11 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         FPB_TMEM_LD32(t_base + j, acc);
         if (has_res && j + 32 < j0 + kSpan) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            rn[g] = *reinterpret_cast<const uint4*>(
-                res + static_cast<long long>((n0 + j + 32 + g * 8) >> 3) * d.res_plane_stride +
-                static_cast<long long>(r) * 16);
-          }
+          for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j + 32 + g * 8, r, rn[g]);
         }
         tmemWaitLd();
         if (valid) {
@@ -389,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (has_res) {
               float rf[8];
-              unpack8<T>(rv[g], rf);
+              unpackRec8<T>(rv[g], rf);
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] += rf[e];
             }
@@ -402,13 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
             }
-            const int cd = ch_base + n;
-            *reinterpret_cast<uint4*>(dst + static_cast<long long>(cd >> 3) * d.dst_plane_stride +
-                                      drow * 16) = pack8<T>(v);
+            storeRec8<T>(dst, d.dst_plane_stride, ch_base + n, drow, v);
           }
         }
 #pragma unroll
-        for (int g = 0; g < 4; ++g) rv[g] = rn[g];
+        for (int g = 0; g < 4; ++g) {
+          rv[g][0] = rn[g][0];
+          rv[g][1] = rn[g][1];
+        }
       }
       tcFenceBefore();
       __syncwarp();
@@ -451,12 +511,14 @@ int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map
   EncodeTiledFn enc = encodeFn();
   if (enc == nullptr) return fail("fpk_gemm: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kprime), static_cast<cuuint64_t>(d.cout)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kprime) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(bn)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kprime) * (d.dtype == FPK_DTYPE_F32 ? 4 : 2)};
+  const int esize = d.dtype == FPK_DTYPE_F32 ? 4 : 2;
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kStageBytes / esize), static_cast<cuuint32_t>(bn)};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map,
-                         d.dtype == FPK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         d.dtype == FPK_DTYPE_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                         : d.dtype == FPK_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                          2, const_cast<void*>(d.w), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -497,6 +559,22 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   return checkLaunch("gemmKernel");
 }
 
+template <typename T>
+int launchShape(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, size_t smem,
+                cudaStream_t s, int bn, int mh) {
+  if (mh == 2) {
+    return bn == 64 ? launch<T, 64, 2>(d, pl, map, smem, s) : launch<T, 128, 2>(d, pl, map, smem, s);
+  }
+  switch (bn) {
+    case 64:
+      return launch<T, 64, 1>(d, pl, map, smem, s);
+    case 128:
+      return launch<T, 128, 1>(d, pl, map, smem, s);
+    default:
+      return launch<T, 256, 1>(d, pl, map, smem, s);
+  }
+}
+
 }  // namespace gemm
 }  // namespace fpb
 
@@ -509,9 +587,15 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     return fail("fpk_gemm: null pointer in descriptor");
   }
   const fpk_gemm_desc_t& d = *desc;
-  if (d.dtype != FPK_DTYPE_F16 && d.dtype != FPK_DTYPE_BF16) return fail("fpk_gemm: dtype must be f16 or bf16");
+  if (d.dtype != FPK_DTYPE_F16 && d.dtype != FPK_DTYPE_BF16 && d.dtype != FPK_DTYPE_F32) {
+    return fail("fpk_gemm: dtype must be f16, bf16 or f32 (TF32 tensor-core math)");
+  }
+  const int esize = d.dtype == FPK_DTYPE_F32 ? 4 : 2;
+  const int stage_elems = kStageBytes / esize;  // 64 (16-bit) or 32 (fp32) channels per chunk
   if (d.taps < 1 || d.taps > FPK_GEMM_MAX_TAPS) return fail("fpk_gemm: taps out of range");
-  if (d.cin < 32 || (d.cin != 32 && d.cin % 64 != 0)) return fail("fpk_gemm: cin must be 32 or a multiple of 64");
+  if (d.cin < 32 || (d.cin != 32 && d.cin % stage_elems != 0)) {
+    return fail("fpk_gemm: cin must be 32 or a multiple of 64 (16-bit) / 32 (f32)");
+  }
   if (d.rows <= 0 || d.img_rows <= 0 || d.grid_w <= 0) return fail("fpk_gemm: bad grid");
   if (reinterpret_cast<uintptr_t>(d.a) % 16 || d.a_plane_stride % 16 ||
       reinterpret_cast<uintptr_t>(d.dst) % 16 || d.dst_plane_stride % 16 ||
@@ -519,11 +603,11 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     return fail("fpk_gemm: pointers and plane strides must be 16-byte aligned");
   }
   Plan pl{};
-  pl.cw = d.cin < 64 ? d.cin : 64;
-  pl.planes = pl.cw / 8;
+  pl.cw = d.cin < stage_elems ? d.cin : stage_elems;
+  pl.planes = pl.cw * esize / 16;
   pl.n_chunks = d.cin / pl.cw;
-  if ((d.taps * pl.cw) % kBlockK != 0) return fail("fpk_gemm: taps*chunk must be a multiple of 64");
-  pl.stages_per_chunk = d.taps * pl.cw / kBlockK;
+  if ((d.taps * pl.cw) % stage_elems != 0) return fail("fpk_gemm: taps*chunk must fill whole 128-byte stages");
+  pl.stages_per_chunk = d.taps * pl.cw / stage_elems;
   if (pl.stages_per_chunk > kMaxStagesPerChunk) return fail("fpk_gemm: too many weight stages per chunk");
   int mn = d.tap_off[0], mx = d.tap_off[0];
   for (int t = 1; t < d.taps; ++t) {
@@ -568,17 +652,12 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   CUtensorMap map;
   if (makeWeightMap(d, kprime, bn, &map) != 0) return 1;
   auto s = static_cast<cudaStream_t>(stream);
-  const bool bf = d.dtype == FPK_DTYPE_BF16;
-  if (mh == 2) {
-    if (bn == 64) return bf ? launch<__nv_bfloat16, 64, 2>(d, pl, map, smem, s) : launch<__half, 64, 2>(d, pl, map, smem, s);
-    return bf ? launch<__nv_bfloat16, 128, 2>(d, pl, map, smem, s) : launch<__half, 128, 2>(d, pl, map, smem, s);
-  }
-  switch (bn) {
-    case 64:
-      return bf ? launch<__nv_bfloat16, 64, 1>(d, pl, map, smem, s) : launch<__half, 64, 1>(d, pl, map, smem, s);
-    case 128:
-      return bf ? launch<__nv_bfloat16, 128, 1>(d, pl, map, smem, s) : launch<__half, 128, 1>(d, pl, map, smem, s);
+  switch (d.dtype) {
+    case FPK_DTYPE_BF16:
+      return launchShape<__nv_bfloat16>(d, pl, map, smem, s, bn, mh);
+    case FPK_DTYPE_F32:
+      return launchShape<float>(d, pl, map, smem, s, bn, mh);
     default:
-      return bf ? launch<__nv_bfloat16, 256, 1>(d, pl, map, smem, s) : launch<__half, 256, 1>(d, pl, map, smem, s);
+      return launchShape<__half>(d, pl, map, smem, s, bn, mh);
   }
 }

@@ -34,17 +34,16 @@ struct LnArgs {
   float eps;
 };
 
-cudaError_t launchAttention(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s);
-// tcgen05 / TMEM attention (fp_attention.cu); same arguments, needs error_flag.
-cudaError_t launchAttentionTc(const AttnArgs& a, int layers, int n_seq, bool bf16, cudaStream_t s);
-cudaError_t launchLayerNorm(const LnArgs& a, bool bf16, cudaStream_t s);
+// tcgen05 / TMEM attention (fp_attention.cu); dtype FPK_DTYPE_*, needs error_flag.
+cudaError_t launchAttentionTc(const AttnArgs& a, int layers, int n_seq, int dtype, cudaStream_t s);
+cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s);
 cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int seq_len, int n_seq,
-                            float* out, bool bf16, cudaStream_t s);
+                            float* out, int dtype, cudaStream_t s);
 cudaError_t launchLinearF32(const float* x, const float* w, const float* b, float* y, int m, int n,
                             int k, bool relu, cudaStream_t s);
 cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStream_t s);
 cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n, int H, int W,
-                             void* dst, long long plane_stride, bool bf16, cudaStream_t s);
+                             void* dst, long long plane_stride, int dtype, cudaStream_t s);
 cudaError_t launchConvert(const float* in, void* out, long long n, bool bf16, cudaStream_t s);
 
 }  // namespace net

@@ -1,7 +1,9 @@
 // RefineNet / ScoreNet forward passes on the sm_100a kernels.
 //
-// Activation layout: KP8 planar buffers (include/fpk.h) on padded spatial
-// grids, so every convolution is one fpk_gemm launch:
+// Activation layout: planar buffers (include/fpk.h; 16-byte records of 8
+// fp16/bf16 or 4 fp32 channels) on padded spatial grids, so every convolution
+// is one fpk_gemm launch. FP16 / BF16 run kind::f16, FP32 and TF32 keep fp32
+// activations and run kind::tf32 (TF32 multiplies, fp32 accumulation):
 //   stem input   space-to-depth of the 160x160x6 crops, grid 83x83, 32 ch
 //   stem 7x7/2   16 taps (4x4) over 32 ch              -> S2D, grid 41x41, 256 ch
 //   conv 3x3/2   4 taps (2x2) over 256 ch              -> grid 41x41 (40x40 valid), 128 ch
@@ -9,7 +11,7 @@
 //   encAB        res blocks at 256 ch, last -> S2D grid 21x21, 1024 ch
 //   conv 3x3/2   4 taps over 1024 ch                   -> grid 21x21 (20x20 valid), 512 ch
 //   res blocks   last -> TOKENS [B*400, 512] + positional embedding
-// Transformer layers run as GEMMs (QKV, out-proj, FF) + attentionKernel +
+// Transformer layers run as GEMMs (QKV, out-proj, FF) + tcgen05 attention +
 // LayerNorm + token mean; ScoreNet's cross-hypothesis attention is fp32.
 #include <cuda_runtime.h>
 
@@ -100,9 +102,10 @@ const std::vector<float>& WeightPack::at(const std::string& name) const {
 
 namespace {
 
-// [cout][taps][cin] -> chunk-major [cout][K'], k' = chunk*(taps*cw) + tap*cw + c.
-std::vector<float> chunkMajor(const std::vector<float>& w3, int cout, int taps, int cin) {
-  const int cw = cin < 64 ? cin : 64;
+// [cout][taps][cin] -> chunk-major [cout][K'], k' = chunk*(taps*cw) + tap*cw + c,
+// with cw = the channels of one 128-byte chunk (64 fp16/bf16, 32 fp32).
+std::vector<float> chunkMajor(const std::vector<float>& w3, int cout, int taps, int cin, int chunk) {
+  const int cw = cin < chunk ? cin : chunk;
   std::vector<float> out(static_cast<size_t>(cout) * taps * cin);
   for (int o = 0; o < cout; ++o)
     for (int t = 0; t < taps; ++t)
@@ -113,6 +116,21 @@ std::vector<float> chunkMajor(const std::vector<float>& w3, int cout, int taps, 
             w3[(static_cast<size_t>(o) * taps + t) * cin + c];
       }
   return out;
+}
+
+// fp32 -> TF32 (round to nearest, ties away from zero; the 13 low mantissa
+// bits become zero) for weights consumed by kind::tf32 MMAs, which would
+// otherwise truncate them.
+std::vector<float> roundTf32(std::vector<float> v) {
+  for (float& x : v) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) {  // finite
+      u = (u + 0x1000u) & ~0x1FFFu;
+      std::memcpy(&x, &u, 4);
+    }
+  }
+  return v;
 }
 
 // Stride-1 kxk conv [cout][cin][k][k] -> [cout][k*k][cin].
@@ -153,8 +171,8 @@ std::vector<float> s2dTaps(const std::vector<float>& w, int cout, int cin, int k
 
 class Network {
  public:
-  Network(const WeightPack& pack, bool bf16, std::vector<void*>& allocs)
-      : bf16_(bf16), allocs_(allocs), arch_(pack.arch) {
+  Network(const WeightPack& pack, int dtype, std::vector<void*>& allocs)
+      : dtype_(dtype), allocs_(allocs), arch_(pack.arch) {
     // Encoder.
     conv("encA.conv1", pack, s2dTaps(pack.at("encA.conv1.w"), 64, 6, 7, 8), 64, 32, 16, offsets(4, kStemGrid),
          2.0 * 64 * 49 * 6);
@@ -236,14 +254,17 @@ class Network {
     return static_cast<float*>(p);
   }
 
-  void* uploadHalf(const std::vector<float>& v) {
+  // Weights in the activation type: fp32 as is, else converted on the device.
+  void* uploadWeights(const std::vector<float>& v) {
+    if (dtype_ == FPK_DTYPE_F32) return upload(roundTf32(v));
     float* tmp = nullptr;
     check(cudaMalloc(&tmp, v.size() * 4), "cudaMalloc staging");
     check(cudaMemcpy(tmp, v.data(), v.size() * 4, cudaMemcpyHostToDevice), "upload staging");
     void* p = nullptr;
     check(cudaMalloc(&p, v.size() * 2 + 16), "cudaMalloc weights");
     allocs_.push_back(p);
-    check(net::launchConvert(tmp, p, static_cast<long long>(v.size()), bf16_, nullptr), "convert weights");
+    check(net::launchConvert(tmp, p, static_cast<long long>(v.size()), dtype_ == FPK_DTYPE_BF16, nullptr),
+          "convert weights");
     check(cudaDeviceSynchronize(), "convert weights");
     cudaFree(tmp);
     return p;
@@ -253,7 +274,7 @@ class Network {
             int cout, int cin, int taps, const std::vector<int>& offs, double flops_per_row) {
     ConvLayer c;
     c.flops_per_row = flops_per_row;
-    c.w = uploadHalf(chunkMajor(taps_w, cout, taps, cin));
+    c.w = uploadWeights(chunkMajor(taps_w, cout, taps, cin, chunk()));
     c.bias = upload(pack.at(name + ".b"));
     c.cin = cin;
     c.cout = cout;
@@ -271,7 +292,7 @@ class Network {
 
   ConvLayer linear(const std::vector<float>& w, const std::vector<float>& b, int cout, int cin) {
     ConvLayer c;
-    c.w = uploadHalf(chunkMajor(w, cout, 1, cin));
+    c.w = uploadWeights(chunkMajor(w, cout, 1, cin, chunk()));
     c.bias = upload(b);
     c.cin = cin;
     c.cout = cout;
@@ -280,7 +301,9 @@ class Network {
     return c;
   }
 
-  bool bf16_;
+  int chunk() const { return dtype_ == FPK_DTYPE_F32 ? 32 : 64; }
+
+  int dtype_;
   std::vector<void*>& allocs_;
   int arch_;
 };
@@ -299,10 +322,12 @@ struct NetworkRunner::Act {
 
 namespace {
 
-Planar allocPlanar(std::vector<void*>& allocs, long long rows, int channels) {
+// Planar buffer of `channels` channels, `per_record` channels per 16-byte
+// record (8 for fp16/bf16, 4 for fp32).
+Planar allocPlanar(std::vector<void*>& allocs, long long rows, int channels, int per_record) {
   Planar p;
   p.rows = rows;
-  p.planes = channels / 8;
+  p.planes = channels / per_record;
   p.plane_stride = ((kGuardPre + rows + kGuardPost) * 16 + 255) / 256 * 256;
   p.bytes = static_cast<size_t>(p.plane_stride) * p.planes;
   check(cudaMalloc(&p.mem, p.bytes), "cudaMalloc activations");
@@ -327,36 +352,34 @@ NetworkRunner::NetworkRunner(const std::string& refine_path, const std::string& 
   if (crop_w != 160 || crop_h != 160) {
     throw std::runtime_error("the built-in RefineNet/ScoreNet require 160x160 crops");
   }
-  if (precision != NetPrecision::kFP16 && precision != NetPrecision::kBF16) {
-    throw std::runtime_error("this build runs the networks in FP16 or BF16 (tensor cores)");
-  }
   if (max_batch <= 0 || max_batch > 1024) throw std::runtime_error("max batch must be in [1, 1024]");
-  const bool bf = precision == NetPrecision::kBF16;
+  const int dt = dtype();
+  const int pr = perRecord();
   try {
     WeightPack rp = WeightPack::load(refine_path);
     WeightPack sp = WeightPack::load(score_path);
     if (rp.arch != 0) throw std::runtime_error(refine_path + " is not a RefineNet pack");
     if (sp.arch != 1) throw std::runtime_error(score_path + " is not a ScoreNet pack");
-    refine_ = std::make_unique<Network>(rp, bf, allocations_);
-    score_ = std::make_unique<Network>(sp, bf, allocations_);
+    refine_ = std::make_unique<Network>(rp, dt, allocations_);
+    score_ = std::make_unique<Network>(sp, dt, allocations_);
     const long long B = max_batch;
     const long long N = 2 * B;
-    stem_ = allocPlanar(allocations_, N * kStemGrid * kStemGrid, 32);
+    stem_ = allocPlanar(allocations_, N * kStemGrid * kStemGrid, 32, pr);
     act_ = std::make_unique<Act>();
     Act& a = *act_;
-    a.x1 = allocPlanar(allocations_, N * kG40 * kG40, 256);
-    for (auto& p : a.e) p = allocPlanar(allocations_, N * kG40 * kG40, 128);
-    for (auto& p : a.ab) p = allocPlanar(allocations_, B * kG40 * kG40, 256);
-    a.x4 = allocPlanar(allocations_, B * kG20 * kG20, 1024);
-    for (auto& p : a.f) p = allocPlanar(allocations_, B * kG20 * kG20, 512);
+    a.x1 = allocPlanar(allocations_, N * kG40 * kG40, 256, pr);
+    for (auto& p : a.e) p = allocPlanar(allocations_, N * kG40 * kG40, 128, pr);
+    for (auto& p : a.ab) p = allocPlanar(allocations_, B * kG40 * kG40, 256, pr);
+    a.x4 = allocPlanar(allocations_, B * kG20 * kG20, 1024, pr);
+    for (auto& p : a.f) p = allocPlanar(allocations_, B * kG20 * kG20, 512, pr);
     const long long T = B * kTokens;
-    a.tok = allocPlanar(allocations_, T, kEmbed);
-    a.qkv = allocPlanar(allocations_, T, 6 * kEmbed);
-    a.att = allocPlanar(allocations_, T, 2 * kEmbed);
-    a.y1 = allocPlanar(allocations_, T, kEmbed);
-    a.x1n = allocPlanar(allocations_, T, kEmbed);
-    a.h = allocPlanar(allocations_, T, kEmbed);
-    a.y2 = allocPlanar(allocations_, T, kEmbed);
+    a.tok = allocPlanar(allocations_, T, kEmbed, pr);
+    a.qkv = allocPlanar(allocations_, T, 6 * kEmbed, pr);
+    a.att = allocPlanar(allocations_, T, 2 * kEmbed, pr);
+    a.y1 = allocPlanar(allocations_, T, kEmbed, pr);
+    a.x1n = allocPlanar(allocations_, T, kEmbed, pr);
+    a.h = allocPlanar(allocations_, T, kEmbed, pr);
+    a.y2 = allocPlanar(allocations_, T, kEmbed, pr);
     a.feat = allocF32(allocations_, 2 * B * kEmbed);
     a.qkvc = allocF32(allocations_, B * 3 * kEmbed);
     a.oc = allocF32(allocations_, B * kEmbed);
@@ -378,8 +401,17 @@ NetworkRunner::~NetworkRunner() {
 }
 
 int NetworkRunner::dtype() const {
-  return precision_ == NetPrecision::kBF16 ? FPK_DTYPE_BF16 : FPK_DTYPE_F16;
+  switch (precision_) {
+    case NetPrecision::kBF16:
+      return FPK_DTYPE_BF16;
+    case NetPrecision::kFP16:
+      return FPK_DTYPE_F16;
+    default:
+      return FPK_DTYPE_F32;  // FP32 and TF32: fp32 activations, TF32 tensor-core math
+  }
 }
+
+int NetworkRunner::perRecord() const { return dtype() == FPK_DTYPE_F32 ? 4 : 8; }
 
 void NetworkRunner::gemm(const ConvLayer& L, const Planar& a, long long a_row0, long long rows,
                          const Planar& dst, int mode, int img_rows, int grid_w, int valid_h,
@@ -453,7 +485,8 @@ void NetworkRunner::refine(int count, int first_chunk, float* delta_t, float* de
   if (count <= 0 || count > max_batch_) throw std::runtime_error("refine batch exceeds the prepared maximum");
   Act& a = *act_;
   const Network& net = *refine_;
-  const bool bf = precision_ == NetPrecision::kBF16;
+  const int dt = dtype();
+  const int pr = perRecord();
   encoder(net, count, static_cast<long long>(first_chunk) * 2 * count * kStemGrid * kStemGrid, s);
   const long long T = static_cast<long long>(count) * kTokens;
   const int t = static_cast<int>(T);
@@ -461,35 +494,35 @@ void NetworkRunner::refine(int count, int first_chunk, float* delta_t, float* de
   net::AttnArgs at{};
   at.qkv = a.qkv.base;
   at.qkv_plane_stride = a.qkv.plane_stride;
-  at.qkv_layer_planes = 3 * kEmbed / 8;
+  at.qkv_layer_planes = 3 * kEmbed / pr;
   at.q_plane = 0;
-  at.k_plane = kEmbed / 8;
-  at.v_plane = 2 * kEmbed / 8;
+  at.k_plane = kEmbed / pr;
+  at.v_plane = 2 * kEmbed / pr;
   at.out = a.att.base;
   at.out_plane_stride = a.att.plane_stride;
-  at.out_layer_planes = kEmbed / 8;
+  at.out_layer_planes = kEmbed / pr;
   at.seq_len = kTokens;
   at.heads = 4;
   at.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
   at.error_flag = err_;
   {
     prof::Scope scope(prof::kAttention, 2.0 * 4 * count * 4.0 * kTokens * kTokens * 128, s);
-    check(net::launchAttentionTc(at, 2, count, bf, s), "attention");
+    check(net::launchAttentionTc(at, 2, count, dt, s), "attention");
   }
   float* outs[2] = {delta_t, delta_r};
   const char* heads[2] = {"trans", "rot"};
   for (int z = 0; z < 2; ++z) {
     const std::string p(heads[z]);
     // y1 = x + out_proj(attention); x1 = LN1(y1); y2 = x1 + FF(x1); z = LN2(y2)
-    gemm(net.L(p + ".out_proj"), a.att, 0, T, a.y1, FPK_DST_SAME, t, 1, t, 1, false, &a.tok, 0, 0, 1, 0, nullptr, s, 0, z * kEmbed / 8);
+    gemm(net.L(p + ".out_proj"), a.att, 0, T, a.y1, FPK_DST_SAME, t, 1, t, 1, false, &a.tok, 0, 0, 1, 0, nullptr, s, 0, z * kEmbed / pr);
     net::LnArgs ln{a.y1.base, a.y1.plane_stride, a.x1n.base, a.x1n.plane_stride, T, net.F(p + ".ln1.w"), net.F(p + ".ln1.b"), 1e-5f};
-    check(net::launchLayerNorm(ln, bf, s), "layernorm");
+    check(net::launchLayerNorm(ln, dt, s), "layernorm");
     gemm(net.L(p + ".ff1"), a.x1n, 0, T, a.h, FPK_DST_SAME, t, 1, t, 1, true, nullptr, 0, 0, 1, 0, nullptr, s);
     gemm(net.L(p + ".ff2"), a.h, 0, T, a.y2, FPK_DST_SAME, t, 1, t, 1, false, &a.x1n, 0, 0, 1, 0, nullptr, s);
     net::LnArgs ln2{a.y2.base, a.y2.plane_stride, a.y1.base, a.y1.plane_stride, T, net.F(p + ".ln2.w"), net.F(p + ".ln2.b"), 1e-5f};
-    check(net::launchLayerNorm(ln2, bf, s), "layernorm");
+    check(net::launchLayerNorm(ln2, dt, s), "layernorm");
     float* feat = a.feat + static_cast<size_t>(z) * max_batch_ * kEmbed;
-    check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, count, feat, bf, s), "token mean");
+    check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, count, feat, dt, s), "token mean");
     check(net::launchLinearF32(feat, net.F(p + ".out.w"), net.F(p + ".out.b"), outs[z], count, 3, kEmbed, false, s), "head");
   }
 }
@@ -498,7 +531,8 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
   if (n <= 0 || n > max_batch_) throw std::runtime_error("score batch exceeds the prepared maximum");
   Act& a = *act_;
   const Network& net = *score_;
-  const bool bf = precision_ == NetPrecision::kBF16;
+  const int dt = dtype();
+  const int pr = perRecord();
   encoder(net, n, 0, s);
   const long long T = static_cast<long long>(n) * kTokens;
   const int t = static_cast<int>(T);
@@ -506,23 +540,23 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
   net::AttnArgs at{};
   at.qkv = a.qkv.base;
   at.qkv_plane_stride = a.qkv.plane_stride;
-  at.qkv_layer_planes = 3 * kEmbed / 8;
+  at.qkv_layer_planes = 3 * kEmbed / pr;
   at.q_plane = 0;
-  at.k_plane = kEmbed / 8;
-  at.v_plane = 2 * kEmbed / 8;
+  at.k_plane = kEmbed / pr;
+  at.v_plane = 2 * kEmbed / pr;
   at.out = a.att.base;
   at.out_plane_stride = a.att.plane_stride;
-  at.out_layer_planes = kEmbed / 8;
+  at.out_layer_planes = kEmbed / pr;
   at.seq_len = kTokens;
   at.heads = 4;
   at.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
   at.error_flag = err_;
   {
     prof::Scope scope(prof::kAttention, 1.0 * 4 * n * 4.0 * kTokens * kTokens * 128, s);
-    check(net::launchAttentionTc(at, 1, n, bf, s), "attention");
+    check(net::launchAttentionTc(at, 1, n, dt, s), "attention");
   }
   gemm(net.L("out_proj"), a.att, 0, T, a.y1, FPK_DST_SAME, t, 1, t, 1, false, nullptr, 0, 0, 1, 0, nullptr, s);
-  check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, n, a.feat, bf, s), "token mean");
+  check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, n, a.feat, dt, s), "token mean");
   // Attention across the n hypotheses (fp32), then the score head.
   check(net::launchLinearF32(a.feat, net.F("att_cross.in_w"), net.F("att_cross.in_b"), a.qkvc, n, 3 * kEmbed, kEmbed, false, s), "cross qkv");
   check(net::launchSmallAttention(a.qkvc, n, a.oc, s), "cross attention");
@@ -533,7 +567,7 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
 void NetworkRunner::loadNchw(const float* rendered, const float* observed, int n, cudaStream_t s) {
   if (n <= 0 || n > max_batch_) throw std::runtime_error("batch exceeds the prepared maximum");
   check(net::launchNchwToStem(rendered, observed, n, crop_h_, crop_w_, stem_.base, stem_.plane_stride,
-                              precision_ == NetPrecision::kBF16, s),
+                              dtype(), s),
         "nchw to stem");
 }
 

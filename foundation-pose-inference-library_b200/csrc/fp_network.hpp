@@ -12,7 +12,7 @@
 
 namespace fpb {
 
-// Guard rows around every plane of a KP8 activation buffer: convolution
+// Guard rows around every plane of a planar activation buffer: convolution
 // windows may start up to kGuardPre rows before row 0 and end kGuardPost rows
 // after the last row (both zero, never written).
 constexpr long long kGuardPre = 256;
@@ -42,7 +42,7 @@ struct WeightPack {
 enum class NetPrecision { kFP32 = 0, kTF32 = 1, kFP16 = 2, kBF16 = 3 };
 
 struct ConvLayer {
-  void* w = nullptr;       // [cout][K'] half precision, chunk-major
+  void* w = nullptr;       // [cout][K'] in the activation type, chunk-major
   float* bias = nullptr;   // [cout]
   int cin = 0, cout = 0, taps = 0;
   int tap_off[FPK_GEMM_MAX_TAPS] = {};
@@ -64,7 +64,8 @@ class NetworkRunner {
   // Stem input for `n` hypotheses (images 0..n-1 rendered, n..2n-1 observed,
   // grouped per micro-batch chunk: see stemImage()).
   const Planar& stem() const { return stem_; }
-  int dtype() const;  // FPK_DTYPE_F16 / FPK_DTYPE_BF16
+  int dtype() const;      // FPK_DTYPE_F16 / FPK_DTYPE_BF16 / FPK_DTYPE_F32 (FP32 and TF32)
+  int perRecord() const;  // channels per 16-byte activation record: 8, or 4 for fp32
   NetPrecision precision() const { return precision_; }
   int maxBatch() const { return max_batch_; }
 

@@ -171,6 +171,16 @@ __device__ __forceinline__ void tmemStoreWait() {
       "r"(r[29]), "r"(r[30]), "r"(r[31])                                                         \
       : "memory")
 
+// fp32 -> TF32 with round-to-nearest (ties away), returned as an fp32 whose
+// low 13 mantissa bits are zero. The tensor core reads fp32 operands of a
+// kind::tf32 MMA by dropping those bits (truncation, biased toward zero), so
+// every fp32 operand is rounded once when it is produced instead.
+__device__ __forceinline__ float tf32Round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tensor-core operand reads through matrix descriptors).
 __device__ __forceinline__ void fenceProxyAsyncSmem() {

@@ -67,6 +67,8 @@ _SIGS = {
     "fpk_apply_deltas": (C.c_int, [_P, _P, _P, C.c_int, C.c_float, C.POINTER(Params), _P]),
     "fpk_select_best": (C.c_int, [_P, _P, C.c_int, C.POINTER(C.c_float), _P, _P]),
     "fpk_gemm": (C.c_int, [_P, _P]),
+    "fpk_attention": (C.c_int, [_P, C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_int, _P, C.c_longlong,
+                                C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
     "fpk_net_create": (C.c_void_p, [C.c_char_p, C.c_char_p, C.c_int, C.c_int]),
     "fpk_net_destroy": (None, [_P]),
     "fpk_net_refine": (C.c_int, [_P, _P, _P, C.c_int, _P, _P, _P]),
@@ -172,6 +174,16 @@ def gemm(fl: "FpkLibrary", desc: GemmDesc, stream=0) -> None:
         _bind_gemm(fl.lib)
         fl._gemm_bound = True
     fl._check(fl.lib.fpk_gemm(C.byref(desc), stream or None), "fpk_gemm")
+
+
+def attention(fl: FpkLibrary, qkv: int, qkv_plane_stride: int, qkv_layer_channels: int, q_channel: int,
+              k_channel: int, v_channel: int, out: int, out_plane_stride: int, out_layer_channels: int,
+              layers: int, heads: int, seq_len: int, n_seq: int, dtype: int, error_flag: int,
+              stream: int | None = None) -> None:
+    """fpk_attention: multi-head self-attention over planar activations (see include/fpk.h)."""
+    fl._check(fl.lib.fpk_attention(qkv, qkv_plane_stride, qkv_layer_channels, q_channel, k_channel, v_channel,
+                                   out, out_plane_stride, out_layer_channels, layers, heads, seq_len, n_seq,
+                                   dtype, error_flag, stream or None), "fpk_attention")
 
 
 class Networks:

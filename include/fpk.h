@@ -146,17 +146,19 @@ FP_API int fpk_select_best(const float* poses, const float* scores, int n, const
 /* ---------------------------------------------------------------------------
  * Tensor-core GEMM / implicit convolution (tcgen05 + TMEM, sm_100a).
  *
- * Activations use the channel-group planar layout ("KP8"): plane p holds
- * channels 8p..8p+7 of every row as one 16-byte record, so row r of plane p
- * is at base + p*plane_stride + r*16 bytes. Every plane carries zeroed guard
- * rows before row 0 and after the last row, so shifted convolution windows
- * may start at negative rows.
+ * Activations use the channel-group planar layout: plane p holds one 16-byte
+ * record per row, channels 8p..8p+7 for fp16/bf16 ("KP8") or 4p..4p+3 for
+ * fp32 ("KP4"), so row r of plane p is at base + p*plane_stride + r*16 bytes.
+ * Every plane carries zeroed guard rows before row 0 and after the last row,
+ * so shifted convolution windows may start at negative rows. fp32 operands run
+ * on the tensor cores as TF32 (tcgen05 kind::tf32), fp32 accumulation.
  *
  * out[r, n] = epilogue( sum_t sum_c A[r + tap_off[t], c] * W[n, t, c] + bias[n] )
  * over rows r of a padded spatial grid (img_rows = grid rows per image,
  * grid_w = grid width; rows whose (gy, gx) falls outside valid_h x valid_w are
  * computed but not stored). W is [cout][K'] with K' = (cin/cw)*taps*cw in
- * chunk-major order: k' = chunk*(taps*cw) + tap*cw + c, cw = min(cin, 64).
+ * chunk-major order: k' = chunk*(taps*cw) + tap*cw + c, cw = min(cin, 64) for
+ * 16-bit types and min(cin, 32) for fp32 (one chunk = 128 bytes of a row).
  * dst_mode selects where row r / channel n lands:
  *   SAME   (r, n)
  *   S2D    space-to-depth for a following stride-2 conv: cell ((gy+1)/2, (gx+1)/2)
@@ -182,7 +184,7 @@ typedef struct fpk_gemm_desc {
   const void* w;
   int cout;
   const float* bias;
-  const void* residual; /* same layout/grid as A (KP8, cout channels), or NULL */
+  const void* residual; /* same layout/grid as A (cout channels), or NULL */
   long long res_plane_stride;
   int relu;
   void* dst;
@@ -191,11 +193,25 @@ typedef struct fpk_gemm_desc {
   int img_rows, grid_w, valid_h, valid_w;
   int dst_img_rows, dst_grid_w, img_mod, ch_step;
   const float* pos;
-  int dtype;       /* FPK_DTYPE_F16 or FPK_DTYPE_BF16 */
+  int dtype;       /* FPK_DTYPE_F16, FPK_DTYPE_BF16 or FPK_DTYPE_F32 (TF32 math) */
   int* error_flag; /* device int32; set non-zero if a pipeline wait times out */
 } fpk_gemm_desc_t;
 
 FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
+
+/* Fused multi-head self-attention on tcgen05/TMEM (head dim 128):
+ * out = softmax(Q K^T / sqrt(128)) V for every (layer, head, sequence), over
+ * planar activations of `dtype` (fp16/bf16 KP8, or fp32 KP4 run as TF32).
+ * Sequence s occupies rows [s*seq_len, (s+1)*seq_len). For layer z and head
+ * h, Q / K / V are the 128 channels starting at channel
+ * z*qkv_layer_channels + {q,k,v}_channel + 128h of `qkv`, and the output goes
+ * to channels z*out_layer_channels + 128h of `out`. Replaces the attention
+ * inside the TensorRT engines behind IInferenceRunner::enqueueRefine /
+ * enqueueScore (reference src/tensorrt_runner.cu:367-407). */
+FP_API int fpk_attention(const void* qkv, long long qkv_plane_stride, int qkv_layer_channels,
+                         int q_channel, int k_channel, int v_channel, void* out,
+                         long long out_plane_stride, int out_layer_channels, int layers, int heads,
+                         int seq_len, int n_seq, int dtype, int* error_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
  * RefineNet / ScoreNet as a unit: the built-in inference backend behind

@@ -29,7 +29,7 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "oracle"))
 from fp_net_ref import NetRef  # noqa: E402
 
 pytestmark = pytest.mark.gpu
-FP16 = 2
+FP32, TF32, FP16 = 0, 1, 2
 
 
 @pytest.fixture(scope="module")
@@ -223,12 +223,13 @@ def reference_register(env, oracle, n_hyp, iters):
     return ref, poses, scores.cpu().numpy()
 
 
-@pytest.mark.parametrize("n_hyp,iters", [(1, 3), (42, 2)])
-def test_register_matches_reference_kernels_and_torch_networks(env, oracle, n_hyp, iters):
+@pytest.mark.parametrize("n_hyp,iters,precision", [(1, 3, FP16), (42, 2, FP16), (42, 2, TF32),
+                                                   (1, 2, FP32)])
+def test_register_matches_reference_kernels_and_torch_networks(env, oracle, n_hyp, iters, precision):
     if not REF_GPU_SO.is_file():
         pytest.skip("reference GPU build (oracle/_ref) not present")
     lib, scene = env["lib"], env["scene"]
-    h, _ = create(env, n_hyp=n_hyp)
+    h, _ = create(env, n_hyp=n_hyp, precision=precision)
     rc, pose, score, err = register(lib, h, view(scene), n_refine=iters)
     assert rc == 0, err
     lib.cdll.fp_destroy(h)
@@ -245,9 +246,29 @@ def test_register_matches_reference_kernels_and_torch_networks(env, oracle, n_hy
     r_err = rot_err_deg(pose, unc[i])
     s = np.sort(scores)[::-1]
     gap = float(s[0] - s[1]) if len(s) > 1 else float("inf")
-    print(f"e2e n={n_hyp}: ours=hyp {i}, reference top-1={ref_idx}; pose dt={t_err_mm:.4f} mm "
+    print(f"e2e n={n_hyp} precision={precision}: ours=hyp {i}, reference top-1={ref_idx}; pose dt={t_err_mm:.4f} mm "
           f"dR={r_err:.4f} deg; score {score:.6f} vs reference {scores[i]:.6f} (top-2 gap {gap:.2e})")
     assert t_err_mm <= 1.0 and r_err <= 0.1
     # Same top-1, unless the reference's own scores tie within fp16 noise.
     assert i == ref_idx or scores[ref_idx] - scores[i] <= 1e-3 * max(1.0, abs(scores[ref_idx]))
-    assert abs(score - scores[i]) <= 1e-2 * max(1.0, abs(scores[i]))
+    tol = 1e-3 if precision in (FP32, TF32) else 1e-2
+    assert abs(score - scores[i]) <= tol * max(1.0, abs(scores[i]))
+
+
+def test_default_config_registers(env):
+    """The reference's default configuration (TF32 networks, 252 hypotheses,
+    batch 252) creates and registers unchanged."""
+    lib, scene = env["lib"], env["scene"]
+    cfg = lib.default_config()
+    assert cfg.tensorrt_precision == TF32
+    cfg.max_image_width, cfg.max_image_height = 640, 480
+    s = [str(env["obj"]).encode(), str(env["refine"]).encode(), str(env["score"]).encode(),
+         str(env["dir"]).encode()]
+    opts = CreateOptions(s[0], 0, 1.0, s[1], s[2], s[3])
+    err = C.create_string_buffer(1024)
+    h = lib.cdll.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
+    assert h, err.value.decode()
+    rc, pose, score, e = register(lib, h, view(scene))
+    assert rc == 0, e
+    assert np.isfinite(pose).all() and np.isfinite(score)
+    lib.cdll.fp_destroy(h)

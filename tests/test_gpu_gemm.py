@@ -1,6 +1,7 @@
 """GPU tests of the tcgen05 implicit-GEMM kernel (fpk_gemm) against torch fp32
-on the same half-precision-rounded operands. Tolerance: 1e-2 of the output's
-max magnitude (fp16/bf16 output rounding; fp32 accumulation)."""
+on the same half-precision-rounded operands (fp16/bf16), or on fp32 operands
+multiplied as TF32. Tolerance: 1e-2 of the output's max magnitude (fp16/bf16
+output rounding or TF32 operand rounding; fp32 accumulation)."""
 from __future__ import annotations
 
 import math
@@ -12,12 +13,12 @@ torch = pytest.importorskip("torch")
 import torch.nn.functional as F  # noqa: E402
 
 from fp_b200.kernels import (FPK_DST_S2D, FPK_DST_SAME, FPK_DST_TOKENS, FPK_DTYPE_BF16,  # noqa: E402
-                             FPK_DTYPE_F16, GemmDesc, gemm)
+                             FPK_DTYPE_F16, FPK_DTYPE_F32, GemmDesc, gemm)
 from kp8_util import Planar  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16}
+DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16, FPK_DTYPE_F32: torch.float32}
 
 
 def make_desc(a: Planar, rows, cin, taps_off, w, cout, dst: Planar, dtype, err, bias=None,
@@ -43,10 +44,11 @@ def make_desc(a: Planar, rows, cin, taps_off, w, cout, dst: Planar, dtype, err, 
     return d
 
 
-def chunk_major(w_taps: torch.Tensor) -> torch.Tensor:
-    """[cout, taps, cin] -> [cout, K'] with k' = chunk*(taps*cw) + tap*cw + c."""
+def chunk_major(w_taps: torch.Tensor, dtype=FPK_DTYPE_BF16) -> torch.Tensor:
+    """[cout, taps, cin] -> [cout, K'] with k' = chunk*(taps*cw) + tap*cw + c and
+    cw = the channels of one 128-byte chunk (64 for 16-bit types, 32 for fp32)."""
     cout, taps, cin = w_taps.shape
-    cw = min(cin, 64)
+    cw = min(cin, 32 if dtype == FPK_DTYPE_F32 else 64)
     return (w_taps.reshape(cout, taps, cin // cw, cw).permute(0, 2, 1, 3)
             .reshape(cout, taps * cin).contiguous())
 
@@ -66,7 +68,9 @@ def err():
                                               (777, 128, 128, FPK_DTYPE_F16),
                                               (2000, 256, 256, FPK_DTYPE_BF16),
                                               (513, 512, 512, FPK_DTYPE_BF16),
-                                              (4096, 512, 1536, FPK_DTYPE_F16)])
+                                              (4096, 512, 1536, FPK_DTYPE_F16),
+                                              (777, 128, 128, FPK_DTYPE_F32),
+                                              (4096, 512, 1536, FPK_DTYPE_F32)])
 def test_plain_gemm(fpk, err, m, cin, cout, dtype):
     g = torch.Generator().manual_seed(m + cin)
     dt = DT[dtype]
@@ -75,7 +79,7 @@ def test_plain_gemm(fpk, err, m, cin, cout, dtype):
     b = torch.randn(cout, generator=g).to(DEV)
     pa = Planar(m, cin, dt).set(A.to(DEV))
     out = Planar(m, cout, dt)
-    w = chunk_major(W.reshape(cout, 1, cin)).to(dt).to(DEV)
+    w = chunk_major(W.reshape(cout, 1, cin), dtype).to(dt).to(DEV)
     gemm(fpk, make_desc(pa, m, cin, [0], w, cout, out, dtype, err, bias=b))
     torch.cuda.synchronize()
     assert err.item() == 0
@@ -93,6 +97,8 @@ def test_plain_gemm(fpk, err, m, cin, cout, dtype):
                                                  (128, 128, 40, FPK_DTYPE_F16, 24),
                                                  (64, 64, 40, FPK_DTYPE_BF16, 24),
                                                  (256, 256, 40, FPK_DTYPE_BF16, 3),
+                                                 (128, 128, 40, FPK_DTYPE_F32, 24),
+                                                 (256, 256, 40, FPK_DTYPE_F32, 3),
                                                  (512, 512, 20, FPK_DTYPE_BF16, 3)])
 def test_conv3x3_residual_relu(fpk, err, cin, cout, hw, dtype, n):
     g = torch.Generator().manual_seed(cin * 7 + hw + n)
@@ -116,7 +122,7 @@ def test_conv3x3_residual_relu(fpk, err, cin, cout, hw, dtype, n):
     pr = Planar(rows, cout, dt).set(to_grid(R).to(DEV))
     out = Planar(rows, cout, dt)
     taps = [(ky - 1) * gw + (kx - 1) for ky in range(3) for kx in range(3)]
-    w = chunk_major(Wt.permute(0, 2, 3, 1).reshape(cout, 9, cin)).to(dt).to(DEV)
+    w = chunk_major(Wt.permute(0, 2, 3, 1).reshape(cout, 9, cin), dtype).to(dt).to(DEV)
     gemm(fpk, make_desc(pa, rows, cin, taps, w, cout, out, dtype, err, bias=b, residual=pr,
                         relu=True, img_rows=img_rows, grid_w=gw, valid_h=H, valid_w=W))
     torch.cuda.synchronize()
@@ -145,7 +151,7 @@ def s2d_weights(Wt: torch.Tensor, stride_taps: int, sub_offset: int) -> torch.Te
     return out
 
 
-@pytest.mark.parametrize("dtype", [FPK_DTYPE_BF16, FPK_DTYPE_F16])
+@pytest.mark.parametrize("dtype", [FPK_DTYPE_BF16, FPK_DTYPE_F16, FPK_DTYPE_F32])
 def test_s2d_stride2_conv(fpk, err, dtype):
     """1x1 layer writing space-to-depth, then a 3x3 stride-2 conv as a 2x2 conv."""
     g = torch.Generator().manual_seed(5)
@@ -165,13 +171,13 @@ def test_s2d_stride2_conv(fpk, err, dtype):
     gw2 = H + 1
     rows2 = n * (H + 1) * gw2
     t2 = Planar(rows2, 4 * c1, dt)
-    w1 = chunk_major(W1.reshape(c1, 1, c1)).to(dt).to(DEV)
+    w1 = chunk_major(W1.reshape(c1, 1, c1), dtype).to(dt).to(DEV)
     gemm(fpk, make_desc(pa, rows1, c1, [0], w1, c1, t2, dtype, err, bias=b1, relu=False,
                         mode=FPK_DST_S2D, img_rows=(H2 + 1) * gw1, grid_w=gw1, valid_h=H2,
                         valid_w=H2, dst_img_rows=(H + 1) * gw2, dst_grid_w=gw2))
     out = Planar(rows2, c2, dt)
     taps = [a * gw2 + bb for a in range(2) for bb in range(2)]
-    w2 = chunk_major(s2d_weights(W2, 2, 1)).to(dt).to(DEV)
+    w2 = chunk_major(s2d_weights(W2, 2, 1), dtype).to(dt).to(DEV)
     gemm(fpk, make_desc(t2, rows2, 4 * c1, taps, w2, c2, out, dtype, err, bias=b2, relu=True,
                         img_rows=(H + 1) * gw2, grid_w=gw2, valid_h=H, valid_w=H))
     torch.cuda.synchronize()
@@ -182,7 +188,7 @@ def test_s2d_stride2_conv(fpk, err, dtype):
     close(got, ref.permute(0, 2, 3, 1))
 
 
-@pytest.mark.parametrize("dtype,n", [(FPK_DTYPE_BF16, 2), (FPK_DTYPE_F16, 8)])
+@pytest.mark.parametrize("dtype,n", [(FPK_DTYPE_BF16, 2), (FPK_DTYPE_F16, 8), (FPK_DTYPE_F32, 8)])
 def test_stem_7x7_stride2(fpk, err, dtype, n):
     """7x7 stride-2 pad-3 conv over 6 channels as a 16-tap conv on the 32-channel
     space-to-depth layout the fused render+pack writes (grid 83 for 160 crops)."""
@@ -204,7 +210,7 @@ def test_stem_7x7_stride2(fpk, err, dtype, n):
     pa = Planar(rows, 32, dt).set(T.reshape(rows, 32).to(DEV))
     Wp = torch.zeros(cout, cin + 2, 7, 7)
     Wp[:, :cin] = Wt
-    w = chunk_major(s2d_weights(Wp, 4, 3)).to(dt).to(DEV)
+    w = chunk_major(s2d_weights(Wp, 4, 3), dtype).to(dt).to(DEV)
     out = Planar(rows, cout, dt)
     taps = [a * gs + bb for a in range(4) for bb in range(4)]
     gemm(fpk, make_desc(pa, rows, 32, taps, w, cout, out, dtype, err, bias=b, relu=True,
