@@ -528,6 +528,11 @@ void NetworkRunner::refine(int count, int first_chunk, float* delta_t, float* de
 }
 
 void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
+  scoreFeatures(n, act_->feat, s);
+  scoreHead(n, act_->feat, scores, s);
+}
+
+void NetworkRunner::scoreFeatures(int n, float* features, cudaStream_t s) {
   if (n <= 0 || n > max_batch_) throw std::runtime_error("score batch exceeds the prepared maximum");
   Act& a = *act_;
   const Network& net = *score_;
@@ -556,9 +561,15 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
     check(net::launchAttentionTc(at, 1, n, dt, s), "attention");
   }
   gemm(net.L("out_proj"), a.att, 0, T, a.y1, FPK_DST_SAME, t, 1, t, 1, false, nullptr, 0, 0, 1, 0, nullptr, s);
-  check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, n, a.feat, dt, s), "token mean");
+  check(net::launchTokenMean(a.y1.base, a.y1.plane_stride, kTokens, n, features, dt, s), "token mean");
+}
+
+void NetworkRunner::scoreHead(int n, const float* features, float* scores, cudaStream_t s) {
+  if (n <= 0 || n > max_batch_) throw std::runtime_error("score batch exceeds the prepared maximum");
+  Act& a = *act_;
+  const Network& net = *score_;
   // Attention across the n hypotheses (fp32), then the score head.
-  check(net::launchLinearF32(a.feat, net.F("att_cross.in_w"), net.F("att_cross.in_b"), a.qkvc, n, 3 * kEmbed, kEmbed, false, s), "cross qkv");
+  check(net::launchLinearF32(features, net.F("att_cross.in_w"), net.F("att_cross.in_b"), a.qkvc, n, 3 * kEmbed, kEmbed, false, s), "cross qkv");
   check(net::launchSmallAttention(a.qkvc, n, a.oc, s), "cross attention");
   check(net::launchLinearF32(a.oc, net.F("att_cross.out_w"), net.F("att_cross.out_b"), a.xc, n, kEmbed, kEmbed, false, s), "cross out");
   check(net::launchLinearF32(a.xc, net.F("linear.w"), net.F("linear.b"), scores, n, 1, kEmbed, false, s), "score head");

@@ -74,6 +74,13 @@ class NetworkRunner {
   void refine(int count, int first_chunk, float* delta_t, float* delta_r, cudaStream_t s);
   // ScoreNet over all n hypotheses (stem laid out as one chunk of n).
   void score(int n, float* scores, cudaStream_t s);
+  // ScoreNet split at its one cross-hypothesis step, for sharded registers:
+  // the per-hypothesis part (encoder, token self-attention, token mean) writes
+  // 512 fp32 features per hypothesis; the head attends across all n of them
+  // (features gathered from every shard) and writes n scores.
+  void scoreFeatures(int n, float* features, cudaStream_t s);
+  void scoreHead(int n, const float* features, float* scores, cudaStream_t s);
+  static constexpr int kFeatureDim = 512;
   // NCHW fp32 inputs (IInferenceRunner seam) -> stem buffer, one chunk of n.
   void loadNchw(const float* rendered, const float* observed, int n, cudaStream_t s);
   // Device error flag of the pipelined kernels (0 = ok).

@@ -303,7 +303,7 @@ struct FoundationPose::Impl {
   bool fused = false;  // built-in renderer + networks: fused render/pack path
   int rotation_count = 0;
   DeviceBuffer rgb, mask, depth_raw, depth_filtered, stats, rotations, poses, prev_pose, boxes;
-  DeviceBuffer dt, dr, scores, best, one;
+  DeviceBuffer dt, dr, scores, best, one, seeded;
   DeviceBuffer rend_rgb, rend_xyz, net_rendered, net_observed;  // seam path only
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
@@ -512,6 +512,7 @@ FoundationPose::FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_opt
   I.dr.allocate(B * 3 * 4);
   I.scores.allocate(B * 4);
   I.best.allocate(18 * 4);
+  I.seeded.allocate(B * 16 * 4);
   I.one.allocate(4);
   const float one = 1.0f;
   checkCuda(cudaMemcpy(I.one.data(), &one, 4, cudaMemcpyHostToDevice), "upload constant");
@@ -564,6 +565,95 @@ void FoundationPose::prepareForBatch(int batch_size) {
   impl_->inference->prepareForBatch(batch_size);
 }
 
+namespace {
+
+// Active hypothesis count of a register call (reference foundation_pose.cpp:330-342 rules).
+int activeHypotheses(const FoundationPose::Impl& I, int n_hypotheses) {
+  int active = n_hypotheses > 0 ? std::min(n_hypotheses, I.rotation_count)
+                                : std::min(I.cfg.n_hypotheses, I.rotation_count);
+  active = std::min(active, I.max_hyp);
+  if (active <= 0) throw FoundationPoseError("No active hypotheses available");
+  return active;
+}
+
+// Micro-batch for refining n hypotheses, with the reference's divisibility
+// and graph-capture rules.
+int refineChunk(const FoundationPose::Impl& I, int n) {
+  const int bs = I.cfg.batch_size > 0 ? I.cfg.batch_size : n;
+  const int eff = std::min(n, bs);
+  if (eff > 0 && n % eff != 0) {
+    throw FoundationPoseError("active_hypotheses (" + std::to_string(n) +
+                              ") must be divisible by batch_size (" + std::to_string(eff) + ")");
+  }
+  if (I.cfg.capture_cuda_graph && eff < n) {
+    throw FoundationPoseError("capture_cuda_graph is not supported when batch_size (" + std::to_string(eff) +
+                              ") < active_hypotheses (" + std::to_string(n) + ")");
+  }
+  return eff;
+}
+
+}  // namespace
+
+void FoundationPose::registerShardBegin(const std::uint8_t* rgb_u8, const float* depth_m,
+                                        const std::uint8_t* mask_u8, int width, int height,
+                                        CameraIntrinsics intrinsics, int n_refine, int n_hypotheses,
+                                        int shard_begin, int shard_count, float* features, float* poses) {
+  Impl& I = *impl_;
+  if (!I.fused) throw FoundationPoseError("sharded register requires the built-in renderer and networks");
+  I.validateFrame(rgb_u8, depth_m, mask_u8, width, height, true);
+  intrinsics = validateIntrinsics(intrinsics);
+  if (features == nullptr || poses == nullptr) throw FoundationPoseError("shard outputs are required");
+  const int iters = n_refine >= 0 ? n_refine : I.cfg.n_refine_iters;
+  const int active = activeHypotheses(I, n_hypotheses);
+  if (shard_begin < 0 || shard_count <= 0 || shard_begin + shard_count > active) {
+    throw FoundationPoseError("shard [" + std::to_string(shard_begin) + ", " +
+                              std::to_string(shard_begin + shard_count) + ") is outside the " +
+                              std::to_string(active) + " active hypotheses");
+  }
+  const int eff = refineChunk(I, shard_count);
+  I.upload(rgb_u8, depth_m, mask_u8, width, height);
+  fpkCheck(fpk_preprocess(I.depth_raw.as<float>(), I.mask.as<uint8_t>(), width, height, toK(intrinsics),
+                          &I.params, I.depth_filtered.as<float>(), nullptr, nullptr, I.stats.as<int32_t>(), I.s()));
+  // Seeding is deterministic, so every shard seeds all hypotheses and keeps its range.
+  fpkCheck(fpk_seed_poses(I.stats.as<int32_t>(), I.rotations.as<float>(), active, toK(intrinsics), &I.params,
+                          nullptr, I.seeded.as<float>(), I.s()));
+  checkCuda(cudaMemcpyAsync(I.poses.data(), I.seeded.as<float>() + 16 * shard_begin,
+                            static_cast<std::size_t>(shard_count) * 64, cudaMemcpyDeviceToDevice, I.s()),
+            "cudaMemcpyAsync shard poses");
+  I.active = shard_count;
+  I.refinementLoop(iters, shard_count, eff, width, height, intrinsics);
+  fpb::NetworkRunner& net = I.builtin_runner->net();
+  const fpk_mesh_t m = meshView(I.dmesh);
+  fpkCheck(fpk_render_pack(&m, I.poses.as<float>(), shard_count, I.rgb.as<uint8_t>(), I.depth_filtered.as<float>(),
+                           width, height, toK(intrinsics), &I.params, I.mesh.diameter, 0.1f, net.dtype(),
+                           net.stem().base, net.stem().plane_stride, I.boxes.as<float>(), I.s()));
+  BuiltinInferenceRunner::run([&] { net.scoreFeatures(shard_count, features, I.s()); });
+  checkCuda(cudaMemcpyAsync(poses, I.poses.data(), static_cast<std::size_t>(shard_count) * 64,
+                            cudaMemcpyDeviceToDevice, I.s()),
+            "cudaMemcpyAsync shard poses out");
+  I.stream->synchronize();
+  I.checkNetworkErrors();
+}
+
+PoseEstimate FoundationPose::registerShardFinish(const float* features, const float* poses, int n_hypotheses) {
+  Impl& I = *impl_;
+  if (!I.fused) throw FoundationPoseError("sharded register requires the built-in renderer and networks");
+  if (features == nullptr || poses == nullptr) throw FoundationPoseError("gathered features and poses are required");
+  if (n_hypotheses <= 0 || n_hypotheses > I.max_hyp) {
+    throw FoundationPoseError("n_hypotheses must be in [1, " + std::to_string(I.max_hyp) + "]");
+  }
+  fpb::NetworkRunner& net = I.builtin_runner->net();
+  BuiltinInferenceRunner::run([&] { net.scoreHead(n_hypotheses, features, I.scores.as<float>(), I.s()); });
+  const float center[3] = {I.mesh.center.x, I.mesh.center.y, I.mesh.center.z};
+  fpkCheck(fpk_select_best(poses, I.scores.as<float>(), n_hypotheses, center, I.best.as<float>(), I.s()));
+  PoseEstimate e = I.readBest();
+  checkCuda(cudaMemcpyAsync(I.prev_pose.data(), poses + 16 * I.last_index, 64, cudaMemcpyDeviceToDevice, I.s()),
+            "cudaMemcpyAsync previous pose");
+  I.stream->synchronize();
+  I.has_prev = true;
+  return e;
+}
+
 PoseEstimate FoundationPose::registerFrame(const std::uint8_t* rgb_u8, const float* depth_m,
                                            const std::uint8_t* mask_u8, int width, int height,
                                            CameraIntrinsics intrinsics, int n_refine, int n_hypotheses) {
@@ -571,21 +661,9 @@ PoseEstimate FoundationPose::registerFrame(const std::uint8_t* rgb_u8, const flo
   I.validateFrame(rgb_u8, depth_m, mask_u8, width, height, true);
   intrinsics = validateIntrinsics(intrinsics);
   const int iters = n_refine >= 0 ? n_refine : I.cfg.n_refine_iters;
-  int active = n_hypotheses > 0 ? std::min(n_hypotheses, I.rotation_count)
-                                : std::min(I.cfg.n_hypotheses, I.rotation_count);
-  active = std::min(active, I.max_hyp);
-  if (active <= 0) throw FoundationPoseError("No active hypotheses available");
+  const int active = activeHypotheses(I, n_hypotheses);
   I.active = active;
-  const int bs = I.cfg.batch_size > 0 ? I.cfg.batch_size : active;
-  const int eff = std::min(active, bs);
-  if (eff > 0 && active % eff != 0) {
-    throw FoundationPoseError("active_hypotheses (" + std::to_string(active) +
-                              ") must be divisible by batch_size (" + std::to_string(eff) + ")");
-  }
-  if (I.cfg.capture_cuda_graph && eff < active) {
-    throw FoundationPoseError("capture_cuda_graph is not supported when batch_size (" + std::to_string(eff) +
-                              ") < active_hypotheses (" + std::to_string(active) + ")");
-  }
+  const int eff = refineChunk(I, active);
   I.upload(rgb_u8, depth_m, mask_u8, width, height);
   fpkCheck(fpk_preprocess(I.depth_raw.as<float>(), I.mask.as<uint8_t>(), width, height, toK(intrinsics),
                           &I.params, I.depth_filtered.as<float>(), nullptr, nullptr, I.stats.as<int32_t>(), I.s()));
@@ -862,6 +940,35 @@ int fp_register_frame(fp_handle_t* handle, const fp_image_view_t* image, int n_r
     writeResult(handle->estimator->registerFrame(image->rgb_u8, image->depth_m, image->mask_u8, image->width,
                                                  image->height, intrinsicsOf(*image), n_refine, n_hypotheses),
                 result);
+    writeError(err, err_size, "");
+    return 0;
+  } catch (const std::exception& e) {
+    writeError(err, err_size, e.what());
+    return 1;
+  }
+}
+
+int fp_register_shard_begin(fp_handle_t* handle, const fp_image_view_t* image, int n_refine, int n_hypotheses,
+                            int shard_begin, int shard_count, float* features, float* poses, char* err,
+                            size_t err_size) {
+  try {
+    if (handle == nullptr || !handle->estimator || image == nullptr) throw FoundationPoseError("Invalid handle or image");
+    handle->estimator->registerShardBegin(image->rgb_u8, image->depth_m, image->mask_u8, image->width,
+                                          image->height, intrinsicsOf(*image), n_refine, n_hypotheses,
+                                          shard_begin, shard_count, features, poses);
+    writeError(err, err_size, "");
+    return 0;
+  } catch (const std::exception& e) {
+    writeError(err, err_size, e.what());
+    return 1;
+  }
+}
+
+int fp_register_shard_finish(fp_handle_t* handle, const float* features, const float* poses, int n_hypotheses,
+                             fp_pose_result_t* result, char* err, size_t err_size) {
+  try {
+    if (handle == nullptr || !handle->estimator) throw FoundationPoseError("Invalid handle");
+    writeResult(handle->estimator->registerShardFinish(features, poses, n_hypotheses), result);
     writeError(err, err_size, "");
     return 0;
   } catch (const std::exception& e) {

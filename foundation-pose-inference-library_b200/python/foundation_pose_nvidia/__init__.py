@@ -18,11 +18,14 @@ from foundation_pose_nvidia.core import (
     RegisterOptions,
     RgbdFrame,
     RuntimeConfig,
+    register_sharded,
+    shard_range,
 )
 from foundation_pose_nvidia.exceptions import FoundationPoseError, LibraryNotFoundError
 
 __all__ = [
     "Estimator", "EstimatorOptions", "FPLibrary", "FoundationPoseError", "LibraryNotFoundError",
     "MultiObjectEstimator", "MultiObjectPoseEstimate", "ObjectSpec", "PoseEstimate", "Precision",
-    "RegisterOptions", "RgbdFrame", "RuntimeConfig", "__version__", "load_library",
+    "RegisterOptions", "RgbdFrame", "RuntimeConfig", "__version__", "load_library", "register_sharded",
+    "shard_range",
 ]

@@ -74,6 +74,10 @@ class FPLibrary:
                                             C.POINTER(PoseResult), C.c_char_p, C.c_size_t]),
             "fp_track_frame": (C.c_int, [_P, C.POINTER(ImageView), C.c_int,
                                          C.POINTER(PoseResult), C.c_char_p, C.c_size_t]),
+            "fp_register_shard_begin": (C.c_int, [_P, C.POINTER(ImageView), C.c_int, C.c_int, C.c_int,
+                                                  C.c_int, _P, _P, C.c_char_p, C.c_size_t]),
+            "fp_register_shard_finish": (C.c_int, [_P, _P, _P, C.c_int, C.POINTER(PoseResult),
+                                                   C.c_char_p, C.c_size_t]),
             "fp_synchronize_device": (C.c_int, [C.c_char_p, C.c_size_t]),
             "fp_build_info": (C.c_char_p, []),
         }

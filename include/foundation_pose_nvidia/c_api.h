@@ -157,6 +157,39 @@ FP_API int fp_track_frame(fp_handle_t* handle,
                           char* error_buffer,
                           size_t error_buffer_size);
 
+/** Sharded register, phase 1 (no counterpart in the reference: the
+ * multi-GPU extension of fp_register_frame). One handle per GPU, all created
+ * from the same mesh and config. Each shard refines hypotheses
+ * [shard_begin, shard_begin + shard_count) of the n_hypotheses seeded for
+ * `image` and writes, into device memory on its handle's GPU, their ScoreNet
+ * features (shard_count x FP_SCORE_FEATURE_DIM floats) and refined
+ * object-centred poses (shard_count x 16 floats). Returns when they are
+ * complete. Requires the built-in renderer and networks. */
+#define FP_SCORE_FEATURE_DIM 512
+FP_API int fp_register_shard_begin(fp_handle_t* handle,
+                                   const fp_image_view_t* image,
+                                   int n_refine,
+                                   int n_hypotheses,
+                                   int shard_begin,
+                                   int shard_count,
+                                   float* features,
+                                   float* poses,
+                                   char* error_buffer,
+                                   size_t error_buffer_size);
+
+/** Sharded register, phase 2: the caller gathers every shard's features and
+ * poses (e.g. an NCCL all-gather) into device memory on this handle's GPU, in
+ * hypothesis order; this runs ScoreNet's cross-hypothesis head and the
+ * arg-max over all n_hypotheses and returns what fp_register_frame would. The
+ * handle can then track. */
+FP_API int fp_register_shard_finish(fp_handle_t* handle,
+                                    const float* features,
+                                    const float* poses,
+                                    int n_hypotheses,
+                                    fp_pose_result_t* result,
+                                    char* error_buffer,
+                                    size_t error_buffer_size);
+
 /** Opaque multi-object group (reference c_api.h:398). */
 typedef struct fp_group fp_group_t;
 

@@ -48,6 +48,24 @@ class FoundationPose {
   PoseEstimate trackFrame(const std::uint8_t* rgb_u8, const float* depth_m, int width, int height,
                           CameraIntrinsics intrinsics, int n_refine = -1);
 
+  // Register split across estimators on several GPUs (no counterpart in the
+  // reference; the multi-GPU form of registerFrame). Every shard takes the
+  // same frame and hypothesis count and refines its contiguous range
+  // [shard_begin, shard_begin + shard_count) of the seeded hypotheses, then
+  // writes, into device memory of this estimator's GPU, its ScoreNet features
+  // (shard_count x kScoreFeatureDim floats) and refined object-centred poses
+  // (shard_count x 16 floats, row-major). Requires the built-in renderer and
+  // networks. Returns after the outputs are complete.
+  static constexpr int kScoreFeatureDim = 512;
+  void registerShardBegin(const std::uint8_t* rgb_u8, const float* depth_m, const std::uint8_t* mask_u8,
+                          int width, int height, CameraIntrinsics intrinsics, int n_refine,
+                          int n_hypotheses, int shard_begin, int shard_count, float* features,
+                          float* poses);
+  // Cross-hypothesis ScoreNet head and arg-max over all n_hypotheses shards'
+  // outputs, concatenated in hypothesis order (device memory on this GPU).
+  // The result (and the pose track continues from) equals registerFrame's.
+  PoseEstimate registerShardFinish(const float* features, const float* poses, int n_hypotheses);
+
   const PreprocessedMesh& mesh() const;
   const Config& config() const;
 

@@ -54,3 +54,64 @@ def test_two_rank_timing_rules():
         assert m == 15.0  # max over ranks, on every rank
         assert total == 504.0
         assert abs(value - 504.0 / 0.015) < 1e-6
+
+
+def test_shard_ranges_cover_hypotheses_in_order():
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "foundation-pose-inference-library_b200" / "python"))
+    from foundation_pose_nvidia import shard_range
+
+    for n in (1, 7, 42, 252):
+        for world in (1, 2, 3, 4, 8):
+            if world > n:
+                continue
+            ranges = [shard_range(n, world, r) for r in range(world)]
+            assert ranges[0][0] == 0
+            for (b0, c0), (b1, _) in zip(ranges, ranges[1:]):
+                assert b0 + c0 == b1
+            assert sum(c for _, c in ranges) == n
+            assert max(c for _, c in ranges) - min(c for _, c in ranges) <= 1
+    assert [shard_range(252, 8, r)[1] for r in range(8)] == [32] * 4 + [31] * 4
+    with pytest.raises(ValueError):
+        shard_range(10, 2, 2)
+
+
+def _shard_worker(rank, world, port, n, q):
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "foundation-pose-inference-library_b200" / "python"))
+    from foundation_pose_nvidia.core.sharded import gather_shards, shard_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        begin, count = shard_range(n, world, rank)
+        per = -(-n // world)
+        # Stand-in for fp_register_shard_begin: row i of the shard carries its
+        # global hypothesis index; padding rows are poison.
+        local = torch.full((per, 4), -1.0)
+        local[:count] = torch.arange(begin, begin + count, dtype=torch.float32)[:, None]
+        full = gather_shards(local, n)
+        q.put((rank, full[:, 0].tolist(), (full[:, 1:] == full[:, :1]).all().item()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n,world", [(42, 2), (11, 3)])
+def test_gather_shards_assembles_hypothesis_order(n, world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    res = [q.get(timeout=5) for _ in range(world)]
+    for _, order, rows_ok in res:
+        assert order == [float(i) for i in range(n)]  # every rank, same order, no padding
+        assert rows_ok
