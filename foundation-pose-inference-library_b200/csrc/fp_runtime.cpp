@@ -178,21 +178,32 @@ void uploadMesh(const Mesh& mesh, DeviceMesh& dst, cudaStream_t s) {
 // Built-in renderer behind the IRenderer seam (fpk_render).
 class BuiltinRenderer final : public IRenderer {
  public:
-  explicit BuiltinRenderer(const Config& c) : params_(toParams(c)) {}
+  explicit BuiltinRenderer(const Config& c) : params_(toParams(c)), max_batch_(std::max(1, c.n_hypotheses)) {}
+  void reserveForMesh(int num_vertices, int) override {
+    const std::size_t bytes = fpk_render_workspace_bytes(max_batch_, num_vertices, &params_);
+    if (bytes > workspace_.bytes()) workspace_.allocate(bytes);
+  }
   void render(const DeviceMesh& mesh, const float* poses, const float* crop_boxes, int batch_size,
               CameraIntrinsics k, int, int, float3* out_rgb, float3* out_xyz,
               cudaStream_t stream) override {
     if (mesh.num_vertices <= 0 || mesh.num_faces <= 0) {
       throw FoundationPoseError("builtin renderer received an empty mesh");
     }
+    const std::size_t need = fpk_render_workspace_bytes(batch_size, mesh.num_vertices, &params_);
+    if (need > workspace_.bytes()) {
+      checkCuda(cudaStreamSynchronize(stream), "renderer workspace resize");
+      workspace_.allocate(need);
+    }
     const fpk_mesh_t m = meshView(mesh);
     fpkCheck(fpk_render(&m, poses, crop_boxes, batch_size, toK(k), &params_,
                         reinterpret_cast<float*>(out_rgb), reinterpret_cast<float*>(out_xyz), nullptr,
-                        stream));
+                        workspace_.data(), workspace_.bytes(), stream));
   }
 
  private:
   fpk_params_t params_;
+  int max_batch_;
+  DeviceBuffer workspace_;
 };
 
 fpb::NetPrecision toNetPrecision(TensorrtPrecision p) {
@@ -304,6 +315,7 @@ struct FoundationPose::Impl {
   int rotation_count = 0;
   DeviceBuffer rgb, mask, depth_raw, depth_filtered, stats, rotations, poses, prev_pose, boxes;
   DeviceBuffer dt, dr, scores, best, one, seeded;
+  DeviceBuffer render_ws;  // fused path: fpk_render_pack workspace for max_hyp hypotheses
   DeviceBuffer rend_rgb, rend_xyz, net_rendered, net_observed;  // seam path only
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
@@ -352,7 +364,7 @@ struct FoundationPose::Impl {
         fpkCheck(fpk_render_pack(&m, poses.as<float>() + 16 * off, c, rgb.as<uint8_t>(),
                                  depth_filtered.as<float>(), w, h, toK(k), &params, mesh.diameter,
                                  cfg.depth_min, net.dtype(), net.stem().base, net.stem().plane_stride,
-                                 boxes.as<float>() + 4 * off, s()));
+                                 boxes.as<float>() + 4 * off, render_ws.data(), render_ws.bytes(), s()));
         BuiltinInferenceRunner::run(
             [&] { net.refine(c, 0, dt.as<float>() + 3 * off, dr.as<float>() + 3 * off, s()); });
       }
@@ -381,7 +393,7 @@ struct FoundationPose::Impl {
       const fpk_mesh_t m = meshView(dmesh);
       fpkCheck(fpk_render_pack(&m, poses.as<float>(), n, rgb.as<uint8_t>(), depth_filtered.as<float>(),
                                w, h, toK(k), &params, mesh.diameter, 0.1f, net.dtype(), net.stem().base,
-                               net.stem().plane_stride, boxes.as<float>(), s()));
+                               net.stem().plane_stride, boxes.as<float>(), render_ws.data(), render_ws.bytes(), s()));
       BuiltinInferenceRunner::run([&] { net.score(n, scores.as<float>(), s()); });
     } else {
       prepareSeamInputs(n, w, h, k, 0.1f);
@@ -526,6 +538,7 @@ FoundationPose::FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_opt
   uploadMesh(I.mesh.centered_mesh, I.dmesh, I.s());
   if (I.dmesh.num_faces >= (1 << 24)) throw FoundationPoseError("meshes are limited to 2^24 triangles");
   I.renderer->reserveForMesh(I.dmesh.num_vertices, I.dmesh.num_faces);
+  if (I.fused) I.render_ws.allocate(fpk_render_workspace_bytes(I.max_hyp, I.dmesh.num_vertices, &I.params));
   std::vector<Mat3f> rots = fpb_host::makeRotationGrid(config);
   if (rots.empty()) throw FoundationPoseError("Rotation grid generation returned no hypotheses");
   if (static_cast<int>(rots.size()) > I.max_hyp) rots.resize(static_cast<std::size_t>(I.max_hyp));
@@ -626,7 +639,8 @@ void FoundationPose::registerShardBegin(const std::uint8_t* rgb_u8, const float*
   const fpk_mesh_t m = meshView(I.dmesh);
   fpkCheck(fpk_render_pack(&m, I.poses.as<float>(), shard_count, I.rgb.as<uint8_t>(), I.depth_filtered.as<float>(),
                            width, height, toK(intrinsics), &I.params, I.mesh.diameter, 0.1f, net.dtype(),
-                           net.stem().base, net.stem().plane_stride, I.boxes.as<float>(), I.s()));
+                           net.stem().base, net.stem().plane_stride, I.boxes.as<float>(), I.render_ws.data(),
+                           I.render_ws.bytes(), I.s()));
   BuiltinInferenceRunner::run([&] { net.scoreFeatures(shard_count, features, I.s()); });
   checkCuda(cudaMemcpyAsync(poses, I.poses.data(), static_cast<std::size_t>(shard_count) * 64,
                             cudaMemcpyDeviceToDevice, I.s()),

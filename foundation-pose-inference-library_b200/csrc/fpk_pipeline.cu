@@ -357,6 +357,11 @@ struct RenderArgs {
   void* net;
   long long plane_stride;
   int grid_w, grid_h;  // stem space-to-depth grid (83 x 83 for 160 x 160 crops)
+  // Workspace: per (hypothesis, vertex) clip position and pixel position,
+  // and the triangle-id map [n][H][W] (rast rows, bottom-up; 0 = background).
+  float4* vclip;
+  float2* vscr;
+  int32_t* ids;
 };
 
 struct TriSetup {
@@ -369,28 +374,32 @@ __device__ __forceinline__ float4 vertexClip(const RenderArgs& a, const HypState
   return clipPosition(cam, hs.box, a.k, a.p.znear, a.p.zfar);
 }
 
-// reference src/builtin_raster_renderer.cu:53-77 (vertex fetch, projection, bbox).
-__device__ __forceinline__ TriSetup setupTriangle(const RenderArgs& a, const HypState& hs,
-                                                  int tri, int width, int height) {
+// Crop box of hypothesis `hyp`: given, or from its pose.
+__device__ __forceinline__ float4 hypothesisBox(const RenderArgs& a, int hyp) {
+  return a.boxes_in != nullptr ? reinterpret_cast<const float4*>(a.boxes_in)[hyp]
+                               : cropBox(a.poses + hyp * 16, a.k, a.diameter, a.p.crop_ratio);
+}
+
+// Triangle setup from the per-vertex workspace; reference
+// src/builtin_raster_renderer.cu:53-77 (vertex fetch, projection, bbox). The
+// vertex pass stored exactly the clip positions and pixel coordinates the
+// reference computes per triangle.
+__device__ __forceinline__ TriSetup setupTriangle(const RenderArgs& a, const float4* vclip,
+                                                  const float2* vscr, int tri, int width, int height) {
   TriSetup s;
   const int i0 = __ldg(a.mesh.faces + 3 * tri + 0);
   const int i1 = __ldg(a.mesh.faces + 3 * tri + 1);
   const int i2 = __ldg(a.mesh.faces + 3 * tri + 2);
-  s.p0 = vertexClip(a, hs, i0);
-  s.p1 = vertexClip(a, hs, i1);
-  s.p2 = vertexClip(a, hs, i2);
-  const float half_w = 0.5f * static_cast<float>(width);
-  const float half_h = 0.5f * static_cast<float>(height);
-  const float x0 = (s.p0.x / s.p0.w + 1.0f) * half_w - 0.5f;
-  const float x1 = (s.p1.x / s.p1.w + 1.0f) * half_w - 0.5f;
-  const float x2 = (s.p2.x / s.p2.w + 1.0f) * half_w - 0.5f;
-  const float y0 = (s.p0.y / s.p0.w + 1.0f) * half_h - 0.5f;
-  const float y1 = (s.p1.y / s.p1.w + 1.0f) * half_h - 0.5f;
-  const float y2 = (s.p2.y / s.p2.w + 1.0f) * half_h - 0.5f;
-  s.min_x = max(0, static_cast<int>(floorf(fminf(fminf(x0, x1), x2))));
-  s.max_x = min(width - 1, static_cast<int>(ceilf(fmaxf(fmaxf(x0, x1), x2))));
-  s.min_y = max(0, static_cast<int>(floorf(fminf(fminf(y0, y1), y2))));
-  s.max_y = min(height - 1, static_cast<int>(ceilf(fmaxf(fmaxf(y0, y1), y2))));
+  s.p0 = __ldg(vclip + i0);
+  s.p1 = __ldg(vclip + i1);
+  s.p2 = __ldg(vclip + i2);
+  const float2 q0 = __ldg(vscr + i0);
+  const float2 q1 = __ldg(vscr + i1);
+  const float2 q2 = __ldg(vscr + i2);
+  s.min_x = max(0, static_cast<int>(floorf(fminf(fminf(q0.x, q1.x), q2.x))));
+  s.max_x = min(width - 1, static_cast<int>(ceilf(fmaxf(fmaxf(q0.x, q1.x), q2.x))));
+  s.min_y = max(0, static_cast<int>(floorf(fminf(fminf(q0.y, q1.y), q2.y))));
+  s.max_y = min(height - 1, static_cast<int>(ceilf(fmaxf(fmaxf(q0.y, q1.y), q2.y))));
   return s;
 }
 
@@ -452,9 +461,9 @@ __device__ __forceinline__ float3 sampleTexture(const float* texture, int width,
 
 // Resolve + deferred shading of one pixel whose z-buffer winner is tri_plus_one;
 // reference src/builtin_raster_renderer.cu:137-171 and raster_kernels.cuh:443-494.
-__device__ __forceinline__ void shadePixel(const RenderArgs& a, const HypState& hs, int tri_plus_one,
-                                           int px, int py, int width, int height, float3& rgb,
-                                           float3& xyz) {
+__device__ __forceinline__ void shadePixel(const RenderArgs& a, const HypState& hs, const float4* vclip,
+                                           int tri_plus_one, int px, int py, int width, int height,
+                                           float3& rgb, float3& xyz) {
   const int tri = tri_plus_one - 1;
   const int i0 = __ldg(a.mesh.faces + 3 * tri + 0);
   const int i1 = __ldg(a.mesh.faces + 3 * tri + 1);
@@ -462,9 +471,9 @@ __device__ __forceinline__ void shadePixel(const RenderArgs& a, const HypState& 
   const float3 c0 = camPosition(hs.pose, loadF3(a.mesh.vertices, i0));
   const float3 c1 = camPosition(hs.pose, loadF3(a.mesh.vertices, i1));
   const float3 c2 = camPosition(hs.pose, loadF3(a.mesh.vertices, i2));
-  const float4 p0 = clipPosition(c0, hs.box, a.k, a.p.znear, a.p.zfar);
-  const float4 p1 = clipPosition(c1, hs.box, a.k, a.p.znear, a.p.zfar);
-  const float4 p2 = clipPosition(c2, hs.box, a.k, a.p.znear, a.p.zfar);
+  const float4 p0 = __ldg(vclip + i0);  // = clipPosition(c0, box, ...), from the vertex pass
+  const float4 p1 = __ldg(vclip + i1);
+  const float4 p2 = __ldg(vclip + i2);
 
   const float fx = (2.0f * px + 1.0f) / static_cast<float>(width) - 1.0f;
   const float fy = (2.0f * py + 1.0f) / static_cast<float>(height) - 1.0f;
@@ -668,8 +677,32 @@ __device__ __forceinline__ void storeS2d(void* net, long long plane_stride, int 
   }
 }
 
-template <RenderOut kOut>
-__global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) {
+// Vertex pass: crop box and, per vertex, clip position and pixel position
+// under each hypothesis (once per vertex instead of once per triangle corner).
+__global__ void __launch_bounds__(256) vertexKernel(RenderArgs a) {
+  __shared__ HypState hs;
+  const int hyp = blockIdx.y;
+  const int tid = threadIdx.x;
+  if (tid < 12) hs.pose[tid] = a.poses[hyp * 16 + tid];
+  if (tid == 0) {
+    hs.box = hypothesisBox(a, hyp);
+    if (a.boxes_out != nullptr && blockIdx.x == 0) reinterpret_cast<float4*>(a.boxes_out)[hyp] = hs.box;
+  }
+  __syncthreads();
+  const int v = blockIdx.x * blockDim.x + tid;
+  const int nv = a.mesh.n_vertices;
+  if (v >= nv) return;
+  const float4 c = vertexClip(a, hs, v);
+  const float half_w = 0.5f * static_cast<float>(a.p.input_width);
+  const float half_h = 0.5f * static_cast<float>(a.p.input_height);
+  const size_t o = static_cast<size_t>(hyp) * nv + v;
+  a.vclip[o] = c;
+  a.vscr[o] = make_float2((c.x / c.w + 1.0f) * half_w - 0.5f, (c.y / c.w + 1.0f) * half_h - 0.5f);
+}
+
+// Raster pass: one CTA per (row band, hypothesis), z-buffer of packed
+// (depth, triangle) keys in shared memory; writes the band's triangle ids.
+__global__ void __launch_bounds__(kRenderThreads, 1) rasterKernel(RenderArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned long long* zbuf = reinterpret_cast<unsigned long long*>(smem_raw);
   const int width = a.p.input_width;
@@ -680,36 +713,20 @@ __global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) 
   const int row1 = min(height, row0 + a.rows_per_band);
   const int band_rows = row1 - row0;
   int* big_list = reinterpret_cast<int*>(smem_raw + static_cast<size_t>(a.rows_per_band) * width * 8);
-  __shared__ HypState hs;
   __shared__ int big_count;
-  __shared__ float lut255[256];
   const int tid = threadIdx.x;
-  if (tid < 256) lut255[tid] = static_cast<float>(tid) / 255.0f;
-
-  if (tid < 12) {
-    hs.pose[tid] = a.poses[hyp * 16 + tid];
-  }
-  if (tid == 0) {
-    big_count = 0;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    hs.box = a.boxes_in != nullptr ? reinterpret_cast<const float4*>(a.boxes_in)[hyp]
-                                   : cropBox(a.poses + hyp * 16, a.k, a.diameter, a.p.crop_ratio);
-    if (a.boxes_out != nullptr && band == 0) {
-      reinterpret_cast<float4*>(a.boxes_out)[hyp] = hs.box;
-    }
-  }
-  for (int i = tid; i < band_rows * width; i += kRenderThreads) {
-    zbuf[i] = ~0ull;
-  }
+  const size_t vbase = static_cast<size_t>(hyp) * a.mesh.n_vertices;
+  const float4* vclip = a.vclip + vbase;
+  const float2* vscr = a.vscr + vbase;
+  if (tid == 0) big_count = 0;
+  for (int i = tid; i < band_rows * width; i += kRenderThreads) zbuf[i] = ~0ull;
   __syncthreads();
 
   const float inv_w = 1.0f / static_cast<float>(width);
   const float inv_h = 1.0f / static_cast<float>(height);
   const int nf = a.mesh.n_faces;
   for (int tri = tid; tri < nf; tri += kRenderThreads) {
-    const TriSetup s = setupTriangle(a, hs, tri, width, height);
+    const TriSetup s = setupTriangle(a, vclip, vscr, tri, width, height);
     const int y_lo = max(s.min_y, row0);
     const int y_hi = min(s.max_y, row1 - 1);
     if (s.min_x > s.max_x || y_lo > y_hi) {
@@ -751,7 +768,7 @@ __global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) 
   const int nbig = min(big_count, kBigListCap);
   for (int b = 0; b < nbig; ++b) {
     const int tri = big_list[b];
-    const TriSetup s = setupTriangle(a, hs, tri, width, height);
+    const TriSetup s = setupTriangle(a, vclip, vscr, tri, width, height);
     const int y_lo = max(s.min_y, row0);
     const int y_hi = min(s.max_y, row1 - 1);
     const int bw = s.max_x - s.min_x + 1;
@@ -765,38 +782,60 @@ __global__ void __launch_bounds__(kRenderThreads, 1) renderKernel(RenderArgs a) 
     }
   }
   __syncthreads();
-
-  // Resolve, shade and emit. Output rows are top-down: y = height - 1 - py.
+  // Resolve: triangle id per pixel (0 = background).
+  int32_t* ids = a.ids + (static_cast<size_t>(hyp) * height + row0) * width;
   for (int i = tid; i < band_rows * width; i += kRenderThreads) {
-    const int py = row0 + i / width;
-    const int px = i % width;
     const unsigned long long key = zbuf[i];
-    const int tri_plus_one = key == ~0ull ? 0 : static_cast<int>(key & 0xFFFFFFFFull);
-    float3 rgb = make_float3(0.0f, 0.0f, 0.0f);
-    float3 xyz = make_float3(0.0f, 0.0f, 0.0f);
-    if (tri_plus_one > 0 && tri_plus_one <= nf) {
-      shadePixel(a, hs, tri_plus_one, px, py, width, height, rgb, xyz);
-    }
-    const int y = height - 1 - py;
-    if constexpr (kOut == RenderOut::kNhwc) {
-      const size_t o = (static_cast<size_t>(hyp) * height + y) * width + px;
-      a.out_rgb[3 * o + 0] = rgb.x;
-      a.out_rgb[3 * o + 1] = rgb.y;
-      a.out_rgb[3 * o + 2] = rgb.z;
-      a.out_xyz[3 * o + 0] = xyz.x;
-      a.out_xyz[3 * o + 1] = xyz.y;
-      a.out_xyz[3 * o + 2] = xyz.z;
-      if (a.tri_ids != nullptr) {
-        a.tri_ids[(static_cast<size_t>(hyp) * height + py) * width + px] = tri_plus_one;
-      }
-    } else {
-      const PackedPixel pk = packPixel(a, hs, px, y, width, height, rgb, xyz, lut255);
-      using T = typename std::conditional<
-          kOut == RenderOut::kS2dF32, float,
-          typename std::conditional<kOut == RenderOut::kS2dF16, __half, __nv_bfloat16>::type>::type;
-      storeS2d<T>(a.net, a.plane_stride, hyp, y, px, a.grid_w, a.grid_h, pk.r);
-      storeS2d<T>(a.net, a.plane_stride, a.n + hyp, y, px, a.grid_w, a.grid_h, pk.o);
-    }
+    const int t = key == ~0ull ? 0 : static_cast<int>(key & 0xFFFFFFFFull);
+    ids[i] = t <= nf ? t : 0;
+  }
+}
+
+// Shade + emit: one thread per crop pixel, all hypotheses (many warps per SM
+// to hide the gathers). Output rows are top-down: y = height - 1 - py.
+constexpr int kShadeThreads = 256;  // also the size of the 1/255 table it fills
+
+template <RenderOut kOut>
+__global__ void __launch_bounds__(kShadeThreads) shadeKernel(RenderArgs a) {
+  __shared__ HypState hs;
+  __shared__ float lut255[256];
+  const int width = a.p.input_width;
+  const int height = a.p.input_height;
+  const int hyp = blockIdx.y;  // grid: (pixel blocks, hypotheses)
+  const int tid = threadIdx.x;
+  lut255[tid] = static_cast<float>(tid) / 255.0f;
+  if (tid < 12) hs.pose[tid] = a.poses[hyp * 16 + tid];
+  if (tid == 0) hs.box = hypothesisBox(a, hyp);
+  __syncthreads();
+  const int rem = blockIdx.x * kShadeThreads + tid;
+  if (rem >= width * height) return;
+  const size_t idx = static_cast<size_t>(hyp) * width * height + rem;
+  const int py = rem / width;
+  const int px = rem - py * width;
+  const int tri_plus_one = a.ids[idx];
+  float3 rgb = make_float3(0.0f, 0.0f, 0.0f);
+  float3 xyz = make_float3(0.0f, 0.0f, 0.0f);
+  if (tri_plus_one > 0) {
+    shadePixel(a, hs, a.vclip + static_cast<size_t>(hyp) * a.mesh.n_vertices, tri_plus_one, px, py, width,
+               height, rgb, xyz);
+  }
+  const int y = height - 1 - py;
+  if constexpr (kOut == RenderOut::kNhwc) {
+    const size_t o = (static_cast<size_t>(hyp) * height + y) * width + px;
+    a.out_rgb[3 * o + 0] = rgb.x;
+    a.out_rgb[3 * o + 1] = rgb.y;
+    a.out_rgb[3 * o + 2] = rgb.z;
+    a.out_xyz[3 * o + 0] = xyz.x;
+    a.out_xyz[3 * o + 1] = xyz.y;
+    a.out_xyz[3 * o + 2] = xyz.z;
+    if (a.tri_ids != nullptr) a.tri_ids[idx] = tri_plus_one;
+  } else {
+    const PackedPixel pk = packPixel(a, hs, px, y, width, height, rgb, xyz, lut255);
+    using T = typename std::conditional<
+        kOut == RenderOut::kS2dF32, float,
+        typename std::conditional<kOut == RenderOut::kS2dF16, __half, __nv_bfloat16>::type>::type;
+    storeS2d<T>(a.net, a.plane_stride, hyp, y, px, a.grid_w, a.grid_h, pk.r);
+    storeS2d<T>(a.net, a.plane_stride, a.n + hyp, y, px, a.grid_w, a.grid_h, pk.o);
   }
 }
 
@@ -996,17 +1035,8 @@ int maxDynamicSmem() {
     cudaGetDevice(&dev);
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    // The output variants differ in static shared memory (only the packing
-    // ones hold the 1/255 table): budget for the largest.
-    size_t stat = 0;
-    const void* kernels[4] = {reinterpret_cast<const void*>(renderKernel<RenderOut::kNhwc>),
-                              reinterpret_cast<const void*>(renderKernel<RenderOut::kS2dF32>),
-                              reinterpret_cast<const void*>(renderKernel<RenderOut::kS2dF16>),
-                              reinterpret_cast<const void*>(renderKernel<RenderOut::kS2dBf16>)};
-    for (const void* k : kernels) {
-      cudaFuncAttributes fa{};
-      if (cudaFuncGetAttributes(&fa, k) == cudaSuccess && fa.sharedSizeBytes > stat) stat = fa.sharedSizeBytes;
-    }
+    cudaFuncAttributes fa{};
+    const size_t stat = cudaFuncGetAttributes(&fa, rasterKernel) == cudaSuccess ? fa.sharedSizeBytes : 1024;
     value = optin - static_cast<int>(stat) - 256;
   }
   return value;
@@ -1033,8 +1063,21 @@ int planBands(const fpk_params_t* p, int n, int* rows_per_band, int* bands) {
   return 0;
 }
 
+// Workspace of one render call: clip positions (16 B) and pixel positions
+// (8 B) per (hypothesis, vertex), triangle ids (4 B) per crop pixel.
+struct RenderWorkspace {
+  size_t clip = 0, scr = 0, ids = 0, total = 0;
+  RenderWorkspace(int n, int nv, int w, int h) {
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    clip = up(static_cast<size_t>(n) * nv * 16);
+    scr = up(static_cast<size_t>(n) * nv * 8);
+    ids = up(static_cast<size_t>(n) * w * h * 4);
+    total = clip + scr + ids;
+  }
+};
+
 template <RenderOut kOut>
-int launchRender(RenderArgs& a, cudaStream_t stream) {
+int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   int rows = 0, nb = 0;
   if (planBands(&a.p, a.n, &rows, &nb) != 0) return 1;
   a.rows_per_band = rows;
@@ -1043,14 +1086,28 @@ int launchRender(RenderArgs& a, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 31 && !(attr_done_mask & (1 << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        renderKernel<kOut>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxDynamicSmem());
+    const cudaError_t e =
+        cudaFuncSetAttribute(rasterKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxDynamicSmem());
     if (e != cudaSuccess) {
       cudaGetLastError();
-      return fail(std::string("renderKernel smem attribute: ") + cudaGetErrorString(e));
+      return fail(std::string("rasterKernel smem attribute: ") + cudaGetErrorString(e));
     }
     attr_done_mask |= 1 << dev;
   }
+  const RenderWorkspace ws(a.n, a.mesh.n_vertices, a.p.input_width, a.p.input_height);
+  void* mem = workspace;
+  if (mem == nullptr) {
+    // No caller workspace: a stream-ordered allocation, released in stream order.
+    const cudaError_t e = cudaMallocAsync(&mem, ws.total, stream);
+    if (e != cudaSuccess) return fail(std::string("render workspace: ") + cudaGetErrorString(e));
+  } else if (workspace_bytes < ws.total || reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
+    return fail("render workspace too small or not 256-byte aligned (need " + std::to_string(ws.total) +
+                " bytes, see fpk_render_workspace_bytes)");
+  }
+  unsigned char* base = static_cast<unsigned char*>(mem);
+  a.vclip = reinterpret_cast<float4*>(base);
+  a.vscr = reinterpret_cast<float2*>(base + ws.clip);
+  a.ids = reinterpret_cast<int32_t*>(base + ws.clip + ws.scr);
   // Algorithmic bytes: mesh once, the frame once (rgb + depth) when packing,
   // and the outputs (NHWC fp32 rgb+xyz, or both packed network inputs).
   const double px = static_cast<double>(a.n) * a.p.input_width * a.p.input_height;
@@ -1058,10 +1115,20 @@ int launchRender(RenderArgs& a, cudaStream_t stream) {
   const double bytes = a.mesh.n_vertices * 36.0 + a.mesh.n_faces * 12.0 +
                        (kOut == RenderOut::kNhwc ? px * 24.0
                                                  : px * 12.0 * elt + a.img_w * static_cast<double>(a.img_h) * 7.0);
-  prof::countLaunch(prof::kRender);
-  prof::Scope scope(prof::kRender, bytes, stream);
-  renderKernel<kOut><<<dim3(nb, a.n), kRenderThreads, smem, stream>>>(a);
-  return checkLaunch("renderKernel");
+  int rc = 0;
+  {
+    prof::countLaunch(prof::kRender);
+    prof::countLaunch(prof::kRender);
+    prof::countLaunch(prof::kRender);
+    prof::Scope scope(prof::kRender, bytes, stream);
+    vertexKernel<<<dim3((a.mesh.n_vertices + 255) / 256, a.n), 256, 0, stream>>>(a);
+    rasterKernel<<<dim3(nb, a.n), kRenderThreads, smem, stream>>>(a);
+    shadeKernel<kOut><<<dim3((a.p.input_width * a.p.input_height + kShadeThreads - 1) / kShadeThreads, a.n),
+                        kShadeThreads, 0, stream>>>(a);
+    rc = checkLaunch("render kernels");
+  }
+  if (workspace == nullptr) cudaFreeAsync(mem, stream);
+  return rc;
 }
 
 int validateMesh(const fpk_mesh_t* m) {
@@ -1144,9 +1211,14 @@ int fpk_crop_boxes(const float* poses, int n, fpk_intrinsics_t k, float diameter
   return checkLaunch("cropBoxesKernel");
 }
 
+size_t fpk_render_workspace_bytes(int n, int n_vertices, const fpk_params_t* p) {
+  if (p == nullptr || n <= 0 || n_vertices <= 0) return 0;
+  return RenderWorkspace(n, n_vertices, p->input_width, p->input_height).total;
+}
+
 int fpk_render(const fpk_mesh_t* mesh, const float* poses, const float* boxes, int n,
                fpk_intrinsics_t k, const fpk_params_t* p, float* out_rgb, float* out_xyz,
-               int32_t* tri_ids, void* stream) {
+               int32_t* tri_ids, void* workspace, size_t workspace_bytes, void* stream) {
   if (validateParams(p) != 0 || validateMesh(mesh) != 0) return 1;
   if (n <= 0) return fail("fpk_render: batch must be positive");
   if (poses == nullptr || boxes == nullptr || out_rgb == nullptr || out_xyz == nullptr) {
@@ -1162,7 +1234,7 @@ int fpk_render(const fpk_mesh_t* mesh, const float* poses, const float* boxes, i
   a.out_rgb = out_rgb;
   a.out_xyz = out_xyz;
   a.tri_ids = tri_ids;
-  return launchRender<RenderOut::kNhwc>(a, static_cast<cudaStream_t>(stream));
+  return launchRender<RenderOut::kNhwc>(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, int height,
@@ -1195,7 +1267,8 @@ int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, int hei
 int fpk_render_pack(const fpk_mesh_t* mesh, const float* poses, int n, const uint8_t* rgb,
                     const float* depth_filtered, int width, int height, fpk_intrinsics_t k,
                     const fpk_params_t* p, float diameter, float invalid_depth_threshold, int dtype,
-                    void* net_input, long long plane_stride, float* boxes, void* stream) {
+                    void* net_input, long long plane_stride, float* boxes, void* workspace,
+                    size_t workspace_bytes, void* stream) {
   if (validateParams(p) != 0 || validateMesh(mesh) != 0) return 1;
   if (n <= 0 || width <= 0 || height <= 0) return fail("fpk_render_pack: bad sizes");
   if ((p->input_width & 1) || (p->input_height & 1)) {
@@ -1224,11 +1297,11 @@ int fpk_render_pack(const fpk_mesh_t* mesh, const float* poses, int n, const uin
   auto s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case FPK_DTYPE_F32:
-      return launchRender<RenderOut::kS2dF32>(a, s);
+      return launchRender<RenderOut::kS2dF32>(a, workspace, workspace_bytes, s);
     case FPK_DTYPE_F16:
-      return launchRender<RenderOut::kS2dF16>(a, s);
+      return launchRender<RenderOut::kS2dF16>(a, workspace, workspace_bytes, s);
     case FPK_DTYPE_BF16:
-      return launchRender<RenderOut::kS2dBf16>(a, s);
+      return launchRender<RenderOut::kS2dBf16>(a, workspace, workspace_bytes, s);
     default:
       return fail("fpk_render_pack: unknown dtype");
   }

@@ -57,13 +57,14 @@ _SIGS = {
                                  _P, _P, _P, _P, _P]),
     "fpk_seed_poses": (C.c_int, [_P, _P, C.c_int, Intrinsics, C.POINTER(Params), _P, _P, _P]),
     "fpk_crop_boxes": (C.c_int, [_P, C.c_int, Intrinsics, C.c_float, C.POINTER(Params), _P, _P]),
+    "fpk_render_workspace_bytes": (C.c_size_t, [C.c_int, C.c_int, C.POINTER(Params)]),
     "fpk_render": (C.c_int, [C.POINTER(Mesh), _P, _P, C.c_int, Intrinsics, C.POINTER(Params),
-                             _P, _P, _P, _P]),
+                             _P, _P, _P, _P, C.c_size_t, _P]),
     "fpk_pack": (C.c_int, [_P, _P, C.c_int, C.c_int, Intrinsics, C.POINTER(Params), _P, _P, _P,
                            _P, C.c_int, C.c_float, C.c_float, _P, _P, _P]),
     "fpk_render_pack": (C.c_int, [C.POINTER(Mesh), _P, C.c_int, _P, _P, C.c_int, C.c_int,
                                   Intrinsics, C.POINTER(Params), C.c_float, C.c_float, C.c_int,
-                                  _P, C.c_longlong, _P, _P]),
+                                  _P, C.c_longlong, _P, _P, C.c_size_t, _P]),
     "fpk_apply_deltas": (C.c_int, [_P, _P, _P, C.c_int, C.c_float, C.POINTER(Params), _P]),
     "fpk_select_best": (C.c_int, [_P, _P, C.c_int, C.POINTER(C.c_float), _P, _P]),
     "fpk_gemm": (C.c_int, [_P, _P]),
@@ -116,9 +117,15 @@ class FpkLibrary:
         self._check(self.lib.fpk_crop_boxes(poses, n, k, diameter, C.byref(params), boxes,
                                             stream or None), "fpk_crop_boxes")
 
-    def render(self, mesh, poses, boxes, n, k, params, out_rgb, out_xyz, tri_ids=0, stream=0):
+    def render_workspace_bytes(self, n, n_vertices, params) -> int:
+        return int(self.lib.fpk_render_workspace_bytes(n, n_vertices, C.byref(params)))
+
+    def render(self, mesh, poses, boxes, n, k, params, out_rgb, out_xyz, tri_ids=0, stream=0,
+               workspace=0, workspace_bytes=0):
+        """workspace 0: the library allocates it stream-ordered for the call."""
         self._check(self.lib.fpk_render(C.byref(mesh), poses, boxes, n, k, C.byref(params),
-                                        out_rgb, out_xyz, tri_ids or None, stream or None),
+                                        out_rgb, out_xyz, tri_ids or None, workspace or None,
+                                        workspace_bytes, stream or None),
                     "fpk_render")
 
     def pack(self, rgb, depth_filtered, width, height, k, params, rend_rgb, rend_xyz, poses,
@@ -129,11 +136,13 @@ class FpkLibrary:
                     "fpk_pack")
 
     def render_pack(self, mesh, poses, n, rgb, depth_filtered, width, height, k, params,
-                    diameter, invalid_threshold, dtype, net, plane_stride, boxes, stream=0):
+                    diameter, invalid_threshold, dtype, net, plane_stride, boxes, stream=0,
+                    workspace=0, workspace_bytes=0):
         self._check(self.lib.fpk_render_pack(C.byref(mesh), poses, n, rgb, depth_filtered, width,
                                              height, k, C.byref(params), diameter,
                                              invalid_threshold, dtype, net, plane_stride,
-                                             boxes or None, stream or None), "fpk_render_pack")
+                                             boxes or None, workspace or None, workspace_bytes,
+                                             stream or None), "fpk_render_pack")
 
     def apply_deltas(self, poses, dt, dr, n, diameter, params, stream=0):
         self._check(self.lib.fpk_apply_deltas(poses, dt, dr, n, diameter, C.byref(params),

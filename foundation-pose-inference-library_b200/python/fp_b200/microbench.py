@@ -115,14 +115,18 @@ def bench_render(args) -> dict:
     boxes = torch.empty((args.batch, 4), device=dev)
     diam = float(np.linalg.norm(mesh.vertices.max(0) - mesh.vertices.min(0)))
 
+    ws_bytes = fpk.render_workspace_bytes(args.batch, v.shape[0], params)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+
     def run():
         fpk.render_pack(m, P.data_ptr(), args.batch, d_rgb.data_ptr(), d_depth.data_ptr(), 640, 480, k,
-                        params, diam, 0.001, FPK_DTYPE_F16, net.base, net.stride, boxes.data_ptr())
+                        params, diam, 0.001, FPK_DTYPE_F16, net.base, net.stride, boxes.data_ptr(),
+                        workspace=ws.data_ptr(), workspace_bytes=ws_bytes)
 
     ms = time_fn(torch, run, args.iters)
     px = args.batch * 160 * 160
     nbytes = v.shape[0] * 36 + f.shape[0] * 12 + 640 * 480 * 7 + px * 12 * 2
-    return {"kernel": "renderKernel<S2dF16>", "batch": args.batch, "faces": int(f.shape[0]), "ms": ms,
+    return {"kernel": "render+pack (vertex, raster, shade kernels), fp16", "batch": args.batch, "faces": int(f.shape[0]), "ms": ms,
             "gbs": nbytes / ms / 1e6, "tris_per_s": args.batch * f.shape[0] / ms * 1e3}
 
 

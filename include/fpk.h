@@ -85,15 +85,22 @@ FP_API int fpk_seed_poses(const int32_t* stats, const float* rotations, int n, f
 FP_API int fpk_crop_boxes(const float* poses, int n, fpk_intrinsics_t k, float diameter,
                           const fpk_params_t* p, float* boxes, void* stream);
 
+/* Device workspace (bytes, 256-byte aligned) of one fpk_render /
+ * fpk_render_pack call over n hypotheses of a mesh with n_vertices vertices:
+ * per (hypothesis, vertex) clip and pixel positions plus the triangle-id map.
+ * Passing workspace = NULL to those calls allocates it stream-ordered per call. */
+FP_API size_t fpk_render_workspace_bytes(int n, int n_vertices, const fpk_params_t* p);
+
 /* Rasterize + shade every hypothesis into its crop: NHWC float3 RGB and camera
  * XYZ, rows top-down. Replaces IRenderer::render / BuiltinRasterRenderer::render
  * (reference src/builtin_raster_renderer.cu:218-281, raster_kernels.cuh:336-495).
  * boxes are read (compute them with fpk_crop_boxes). tri_ids (optional,
  * [n*H*W] int32, rows bottom-up like the reference rast buffer) receives
- * triangle_index+1, 0 = background. */
+ * triangle_index+1, 0 = background. Three launches: vertex transform,
+ * shared-memory z-buffer raster, pixel-parallel shading. */
 FP_API int fpk_render(const fpk_mesh_t* mesh, const float* poses, const float* boxes, int n,
                       fpk_intrinsics_t k, const fpk_params_t* p, float* out_rgb, float* out_xyz,
-                      int32_t* tri_ids, void* stream);
+                      int32_t* tri_ids, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Crop-warp + normalisation into the two NCHW [n,6,H,W] fp32 network inputs.
  * Replaces prepareNetworkInputsOnDevice (reference src/cuda_pipeline.cu:434-511, 828-845).
@@ -104,8 +111,9 @@ FP_API int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, 
                     float diameter, float invalid_depth_threshold, float* net_rendered,
                     float* net_observed, void* stream);
 
-/* Fused crop boxes + rasterize + shade + crop-warp + pack: one CTA per
- * (hypothesis, row band), z-buffer resident in shared memory, writing both
+/* Crop boxes + rasterize + shade + crop-warp + pack (vertex transform,
+ * shared-memory z-buffer raster per (hypothesis, row band), pixel-parallel
+ * shading + packing), writing both
  * network inputs straight into the stem's space-to-depth KP8 layout: crop pixel
  * (y, x) of image i (rendered i = 0..n-1, observed n+i) goes to plane
  * ((y+3)%2)*2 + (x+3)%2, row i*gh*gw + ((y+3)/2)*gw + (x+3)/2 with
@@ -119,7 +127,8 @@ FP_API int fpk_render_pack(const fpk_mesh_t* mesh, const float* poses, int n,
                            const uint8_t* rgb, const float* depth_filtered, int width, int height,
                            fpk_intrinsics_t k, const fpk_params_t* p, float diameter,
                            float invalid_depth_threshold, int dtype, void* net_input,
-                           long long plane_stride, float* boxes, void* stream);
+                           long long plane_stride, float* boxes, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Host-only mesh ingest: load an OBJ/PLY, scale by mesh_unit_scale, compute
  * normals when missing, centre on the bounding-box centre and measure the
