@@ -39,6 +39,9 @@ PKG = ROOT / "foundation-pose-inference-library_b200"
 sys.path.insert(0, str(PKG / "python"))
 
 N_HYP = 252
+# gemmKernel DRAM traffic per TFLOP of algorithmic GEMM work, from one ncu
+# capture over whole register calls (profiles/gemm_dram_traffic_register.md).
+GEMM_DRAM_BYTES_PER_TFLOP = 11463.6e6 / 11.60
 N_ITERS = 5
 W, H = 640, 480
 FP16 = 2
@@ -249,7 +252,14 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--track-frames", type=int, default=50)
     ap.add_argument("--e2e-steps", type=int, default=None, help="host-buffer steps (default: --steps)")
+    ap.add_argument("--hyp", type=int, default=252,
+                    help="hypotheses per register; values other than 252 are for profiling captures only "
+                         "(the workload line then names the reduced count)")
     args = ap.parse_args()
+    global N_HYP, WORKLOAD
+    if args.hyp != N_HYP:
+        N_HYP = args.hyp
+        WORKLOAD = WORKLOAD.replace("252 hyp", f"{N_HYP} hyp (profiling)").replace("batch 252", f"batch {N_HYP}")
     if args.impl == "reference":
         run_reference_arm(args)
         return
@@ -420,7 +430,11 @@ def main() -> None:
             "roofline": {"kernel": "gemmKernel (tcgen05 implicit-GEMM conv/linear)", "bound": "tensor",
                          "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s",
                          "frac": (achieved / pk["bf16"]) if achieved else None, "peak_note": pk["note"] + " (sustained bf16)",
-                         "traffic": None, "launches_timed": gemm_n, "gemm_ms_per_step": gemm_ms / args.steps,
+                         "traffic": GEMM_DRAM_BYTES_PER_TFLOP * (gemm_flops / 1e12) / max(1, gemm_n),
+                         "traffic_note": "DRAM bytes per launch (read + write) from one ncu capture of whole "
+                                         "register calls (profiles/gemm_dram_traffic_register.md), scaled by the "
+                                         "launch's average work",
+                         "launches_timed": gemm_n, "gemm_ms_per_step": gemm_ms / args.steps,
                          "gemm_tflop_per_step": gemm_flops / args.steps / 1e12},
             "render_pack": {"ms_per_step": render_ms / args.steps,
                             "achieved_gbs": render_bytes / (render_ms / 1000.0) / 1e9 if render_ms > 0 else None,
