@@ -252,6 +252,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--track-frames", type=int, default=50)
     ap.add_argument("--e2e-steps", type=int, default=None, help="host-buffer steps (default: --steps)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="capture_cuda_graph=0; by default the refinement pass replays as one CUDA graph "
+                         "(capture_cuda_graph=1, the reference's own Config option)")
     ap.add_argument("--hyp", type=int, default=252,
                     help="hypotheses per register; values other than 252 are for profiling captures only "
                          "(the workload line then names the reduced count)")
@@ -293,6 +296,7 @@ def main() -> None:
     cfg = lib.default_config()
     cfg.n_hypotheses, cfg.n_refine_iters, cfg.batch_size = N_HYP, N_ITERS, N_HYP
     cfg.tensorrt_precision = FP16
+    cfg.capture_cuda_graph = 1 if args.graph else 0
     cfg.max_image_width, cfg.max_image_height = W, H
     strs = [str(obj).encode(), str(refine).encode(), str(score).encode(), str(work).encode()]
     opts = CreateOptions(strs[0], local, 1.0, strs[1], strs[2], strs[3])
@@ -421,6 +425,7 @@ def main() -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded scene; random-init weights)",
             "config": {"workload": WORKLOAD, "global_batch": N_HYP, "register_ms": ms_per_step,
                        "l2": "not flushed: each register streams ~2.5 GB of activations (> 126 MB L2)",
+                       "cuda_graph": bool(args.graph),
                        "parallelism": ("single GPU" if world == 1 else
                                        f"hypothesis shards x{world} ({N_HYP // world}-{per} per GPU), NCCL all-gather "
                                        "of ScoreNet features + refined poses, cross-hypothesis head on every rank")},

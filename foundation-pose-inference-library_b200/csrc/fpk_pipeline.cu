@@ -384,12 +384,12 @@ __device__ __forceinline__ float4 hypothesisBox(const RenderArgs& a, int hyp) {
 // src/builtin_raster_renderer.cu:53-77 (vertex fetch, projection, bbox). The
 // vertex pass stored exactly the clip positions and pixel coordinates the
 // reference computes per triangle.
-__device__ __forceinline__ TriSetup setupTriangle(const RenderArgs& a, const float4* vclip,
-                                                  const float2* vscr, int tri, int width, int height) {
+__device__ __forceinline__ TriSetup setupTriangle(const float4* vclip, const float2* vscr, int3 f,
+                                                  int width, int height) {
   TriSetup s;
-  const int i0 = __ldg(a.mesh.faces + 3 * tri + 0);
-  const int i1 = __ldg(a.mesh.faces + 3 * tri + 1);
-  const int i2 = __ldg(a.mesh.faces + 3 * tri + 2);
+  const int i0 = f.x;
+  const int i1 = f.y;
+  const int i2 = f.z;
   s.p0 = __ldg(vclip + i0);
   s.p1 = __ldg(vclip + i1);
   s.p2 = __ldg(vclip + i2);
@@ -401,6 +401,16 @@ __device__ __forceinline__ TriSetup setupTriangle(const RenderArgs& a, const flo
   s.min_y = max(0, static_cast<int>(floorf(fminf(fminf(q0.y, q1.y), q2.y))));
   s.max_y = min(height - 1, static_cast<int>(ceilf(fmaxf(fmaxf(q0.y, q1.y), q2.y))));
   return s;
+}
+
+__device__ __forceinline__ int3 loadFace(const RenderArgs& a, int tri) {
+  return make_int3(__ldg(a.mesh.faces + 3 * tri + 0), __ldg(a.mesh.faces + 3 * tri + 1),
+                   __ldg(a.mesh.faces + 3 * tri + 2));
+}
+
+__device__ __forceinline__ TriSetup setupTriangle(const RenderArgs& a, const float4* vclip,
+                                                  const float2* vscr, int tri, int width, int height) {
+  return setupTriangle(vclip, vscr, loadFace(a, tri), width, height);
 }
 
 // Coverage + depth key for one pixel; reference builtin_raster_renderer.cu:85-111.
@@ -725,8 +735,13 @@ __global__ void __launch_bounds__(kRenderThreads, 1) rasterKernel(RenderArgs a) 
   const float inv_w = 1.0f / static_cast<float>(width);
   const float inv_h = 1.0f / static_cast<float>(height);
   const int nf = a.mesh.n_faces;
+  // The next triangle's indices are loaded one round ahead, so each round
+  // waits on one dependent load (the vertices) instead of two.
+  int3 next_face = tid < nf ? loadFace(a, tid) : make_int3(0, 0, 0);
   for (int tri = tid; tri < nf; tri += kRenderThreads) {
-    const TriSetup s = setupTriangle(a, vclip, vscr, tri, width, height);
+    const int3 face = next_face;
+    if (tri + kRenderThreads < nf) next_face = loadFace(a, tri + kRenderThreads);
+    const TriSetup s = setupTriangle(vclip, vscr, face, width, height);
     const int y_lo = max(s.min_y, row0);
     const int y_hi = min(s.max_y, row1 - 1);
     if (s.min_x > s.max_x || y_lo > y_hi) {
