@@ -218,7 +218,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = d.error_flag;
-  constexpr uint32_t kTmemCols = 2 * MH * BN;
+  // Accumulator buffers: two (the epilogue of tile i overlaps the MMAs of
+  // tile i+1) when they fit the 512 TMEM columns, else one (256-row tiles of
+  // 256 columns, used for the 1x1 linears).
+  constexpr int kBufs = 2 * MH * BN <= 512 ? 2 : 1;
+  constexpr uint32_t kTmemCols = kBufs * MH * BN;
   constexpr int kTileM = kBlockM * MH;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 
@@ -327,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t a_phase = 0, b_phase = 0, t_iter = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++t_iter) {
-        const int buf = t_iter & 1;
-        ok = waitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 13);
+        const int buf = static_cast<int>(t_iter % kBufs);
+        ok = waitBar(&sm->acc_empty[buf], ((t_iter / kBufs) & 1) ^ 1, err, 13);
         if (!ok) break;
         tcFenceAfter();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * MH * BN);
@@ -380,8 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t_iter) {
       const int m0 = (tile / pl.n_tiles) * kTileM;
       const int n0 = (tile % pl.n_tiles) * BN;
-      const int buf = t_iter & 1;
-      if (!waitBar(&sm->acc_full[buf], (t_iter >> 1) & 1, err, 17)) break;
+      const int buf = static_cast<int>(t_iter % kBufs);
+      if (!waitBar(&sm->acc_full[buf], (t_iter / kBufs) & 1, err, 17)) break;
       tcFenceAfter();
       const int r = m0 + row_in_tile;
       bool valid = r < d.rows;
@@ -563,7 +567,14 @@ template <typename T>
 int launchShape(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, size_t smem,
                 cudaStream_t s, int bn, int mh) {
   if (mh == 2) {
-    return bn == 64 ? launch<T, 64, 2>(d, pl, map, smem, s) : launch<T, 128, 2>(d, pl, map, smem, s);
+    switch (bn) {
+      case 64:
+        return launch<T, 64, 2>(d, pl, map, smem, s);
+      case 128:
+        return launch<T, 128, 2>(d, pl, map, smem, s);
+      default:
+        return launch<T, 256, 2>(d, pl, map, smem, s);
+    }
   }
   switch (bn) {
     case 64:
@@ -641,7 +652,12 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   // Narrow layers (BN <= 128) take 256-row tiles when there are enough rows
   // to keep every SM busy.
   int mh = 1;
-  if (bn <= 128 && (d.rows + kBlockM - 1) / kBlockM >= 2 * numSms() && plan(2)) {
+  // 1x1 layers (linears) with 256-column tiles take 256-row tiles too (one
+  // accumulator buffer): every activation window then feeds two MMAs per
+  // weight stage, which their per-stage copies otherwise saturate shared
+  // memory with.
+  const bool wide_linear = bn == 256 && d.taps == 1;
+  if ((bn <= 128 || wide_linear) && (d.rows + kBlockM - 1) / kBlockM >= 2 * numSms() && plan(2)) {
     mh = 2;
   } else if (!plan(1)) {
     return fail("fpk_gemm: activation window too large for shared memory");

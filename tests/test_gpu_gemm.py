@@ -70,7 +70,11 @@ def err():
                                               (513, 512, 512, FPK_DTYPE_BF16),
                                               (4096, 512, 1536, FPK_DTYPE_F16),
                                               (777, 128, 128, FPK_DTYPE_F32),
-                                              (4096, 512, 1536, FPK_DTYPE_F32)])
+                                              (4096, 512, 1536, FPK_DTYPE_F32),
+                                              # > 2 x 148 tiles of 128 rows: 256-row tiles with
+                                              # one accumulator buffer for 1x1 layers
+                                              (40000, 512, 768, FPK_DTYPE_F16),
+                                              (40000, 256, 512, FPK_DTYPE_F32)])
 def test_plain_gemm(fpk, err, m, cin, cout, dtype):
     g = torch.Generator().manual_seed(m + cin)
     dt = DT[dtype]
