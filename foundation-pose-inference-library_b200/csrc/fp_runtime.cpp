@@ -9,9 +9,11 @@
 // with no host synchronisation until the final pose read. Injected IRenderer /
 // IInferenceRunner backends are driven through the reference's NCHW fp32 seam.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <exception>
 #include <format>
@@ -205,6 +207,65 @@ class BuiltinRenderer final : public IRenderer {
   int max_batch_;
   DeviceBuffer workspace_;
 };
+
+// Default-renderer selection (reference src/foundation_pose.cpp:40-68): the
+// built-in rasterizer unless FP_RENDERER=nvdiffrast, which loads the renderer
+// plugin libfoundation_pose_nvdiffrast.so with dlopen and builds the renderer
+// through its extern "C" factory
+//   IRenderer* fp_plugin_create_renderer(const Config*, int device_id, int max_batch).
+// The plugin is looked up on the dynamic loader's path first, then in the
+// directory of this library. It is loaded once per process and never unloaded
+// (renderers it created may outlive any estimator).
+constexpr const char* kRendererPluginName = "libfoundation_pose_nvdiffrast.so";
+using PluginRendererFactory = IRenderer* (*)(const Config*, int, int);
+
+struct RendererPlugin {
+  void* handle = nullptr;
+  std::string error;
+};
+
+const RendererPlugin& rendererPlugin() {
+  static const RendererPlugin plugin = [] {
+    RendererPlugin p;
+    p.handle = dlopen(kRendererPluginName, RTLD_NOW | RTLD_LOCAL);
+    if (p.handle != nullptr) return p;
+    const char* first = dlerror();
+    p.error = first != nullptr ? first : "not found";
+    Dl_info self{};
+    if (dladdr(reinterpret_cast<const void*>(&rendererPlugin), &self) != 0 && self.dli_fname != nullptr) {
+      std::string dir(self.dli_fname);
+      const std::size_t slash = dir.rfind('/');
+      dir = slash == std::string::npos ? std::string(".") : dir.substr(0, slash);
+      p.handle = dlopen((dir + "/" + kRendererPluginName).c_str(), RTLD_NOW | RTLD_LOCAL);
+      if (p.handle == nullptr) {
+        const char* second = dlerror();
+        if (second != nullptr) p.error += std::string("; ") + second;
+      }
+    }
+    return p;
+  }();
+  return plugin;
+}
+
+std::unique_ptr<IRenderer> makeDefaultRenderer(const Config& config, int device_id, int max_batch) {
+  const char* choice = std::getenv("FP_RENDERER");
+  if (choice == nullptr || std::string_view(choice) != "nvdiffrast") {
+    return std::make_unique<BuiltinRenderer>(config);
+  }
+  const RendererPlugin& plugin = rendererPlugin();
+  if (plugin.handle == nullptr) {
+    throw FoundationPoseError(
+        "FP_RENDERER=nvdiffrast requested but the renderer plugin could not be loaded (keep " +
+        std::string(kRendererPluginName) + " on the loader path or next to the main library): " + plugin.error);
+  }
+  auto factory = reinterpret_cast<PluginRendererFactory>(dlsym(plugin.handle, "fp_plugin_create_renderer"));
+  if (factory == nullptr) {
+    throw FoundationPoseError("nvdiffrast renderer plugin is missing fp_plugin_create_renderer");
+  }
+  std::unique_ptr<IRenderer> renderer(factory(&config, device_id, max_batch));
+  if (!renderer) throw FoundationPoseError("nvdiffrast renderer plugin failed to create a renderer");
+  return renderer;
+}
 
 fpb::NetPrecision toNetPrecision(TensorrtPrecision p) {
   switch (p) {
@@ -483,7 +544,8 @@ int maxHypothesesFor(const Config& c) { return std::max(1, c.n_hypotheses); }
 FoundationPose::FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_options, Config config)
     : FoundationPose(std::move(mesh), runtime_options,
                      std::make_unique<BuiltinInferenceRunner>(runtime_options, config, maxHypothesesFor(config)),
-                     std::make_unique<BuiltinRenderer>(config), config) {}
+                     makeDefaultRenderer(config, runtime_options.device_id, maxHypothesesFor(config)),
+                     config) {}
 
 FoundationPose::FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_options,
                                std::unique_ptr<IInferenceRunner> inference_runner,
