@@ -47,8 +47,8 @@ constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, each takes half
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kBlockM = 128;
 constexpr int kStageBytes = 128;  // K bytes per weight stage: 64 fp16/bf16 or 32 fp32 elements
-constexpr int kMaxASlots = 4;
-constexpr int kMaxBStages = 8;
+constexpr int kMaxASlots = 8;
+constexpr int kMaxBStages = 16;
 constexpr int kMaxStagesPerChunk = FPK_GEMM_MAX_TAPS;  // 64-channel chunks: one stage per tap
 constexpr size_t kSmemBytes = 220 * 1024;  // dynamic shared memory per CTA
 
@@ -108,6 +108,7 @@ struct Plan {
   int m_tiles, n_tiles;
   uint32_t a_win_bytes;  // per slot
   uint32_t b_stage_bytes;
+  uint32_t a_slot_bytes;  // CTA-pair kernel: window slot stride (1024-byte aligned)
 };
 
 template <typename T>
@@ -198,6 +199,98 @@ __device__ __forceinline__ void storeRec8(unsigned char* base, long long plane_s
         make_float4(tf32Round(v[4]), tf32Round(v[5]), tf32Round(v[6]), tf32Round(v[7]));
   } else {
     *reinterpret_cast<uint4*>(q) = pack8<T>(v);
+  }
+}
+
+// Epilogue of one accumulator row: converts TMEM columns [j0, j0 + kSpan) of
+// output row r (tile columns from n0) with bias / residual / ReLU / positional
+// embedding and stores them into the destination layout of the layer. t_base
+// is the TMEM address of this warp's lane quarter at column 0 of the row block.
+template <typename T, int kSpan>
+__device__ __forceinline__ void epilogueRow(const fpk_gemm_desc_t& d, uint32_t t_base, int r, int n0, int j0) {
+  const unsigned char* res = static_cast<const unsigned char*>(d.residual);
+  unsigned char* dst = static_cast<unsigned char*>(d.dst);
+  bool valid = r < d.rows;
+  long long drow = 0;
+  int ch_base = 0;
+  int pos_row = 0;
+  if (valid) {
+    const int img = r / d.img_rows;
+    const int loc = r - img * d.img_rows;
+    const int gy = loc / d.grid_w;
+    const int gx = loc - gy * d.grid_w;
+    valid = gy < d.valid_h && gx < d.valid_w;
+    switch (d.dst_mode) {
+      case FPK_DST_S2D:
+        drow = static_cast<long long>(img) * d.dst_img_rows + ((gy + 1) >> 1) * d.dst_grid_w +
+               ((gx + 1) >> 1);
+        ch_base = (((gy + 1) & 1) * 2 + ((gx + 1) & 1)) * d.cout;
+        break;
+      case FPK_DST_CONCAT:
+        drow = static_cast<long long>(img % d.img_mod) * d.img_rows + loc;
+        ch_base = (img / d.img_mod) * d.ch_step;
+        break;
+      case FPK_DST_TOKENS:
+        drow = static_cast<long long>(img) * d.valid_h * d.valid_w + gy * d.valid_w + gx;
+        pos_row = gy * d.valid_w + gx;
+        break;
+      default:
+        drow = r;
+    }
+  }
+  const bool has_res = valid && res != nullptr;
+  // Residual rows of the next 32 columns are fetched while the current
+  // 32 are converted and stored.
+  uint4 rv[4][2] = {}, rn[4][2] = {};
+  if (has_res) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j0 + g * 8, r, rv[g]);
+  }
+#pragma unroll 1
+  for (int j = j0; j < j0 + kSpan; j += 32) {
+    uint32_t acc[32];
+    FPB_TMEM_LD32(t_base + j, acc);
+    if (has_res && j + 32 < j0 + kSpan) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j + 32 + g * 8, r, rn[g]);
+    }
+    tmemWaitLd();
+    if (valid) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int n = n0 + j + g * 8;
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[g * 8 + e]);
+        if (d.bias != nullptr) {
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(d.bias + n));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(d.bias + n + 4));
+          v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+          v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+        }
+        if (has_res) {
+          float rf[8];
+          unpackRec8<T>(rv[g], rf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] += rf[e];
+        }
+        if (d.relu) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = fmaxf(v[e], 0.0f);
+        }
+        if (d.dst_mode == FPK_DST_TOKENS && d.pos != nullptr) {
+          const float* pp = d.pos + static_cast<long long>(pos_row) * d.cout + n;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
+        }
+        storeRec8<T>(dst, d.dst_plane_stride, ch_base + n, drow, v);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      rv[g][0] = rn[g][0];
+      rv[g][1] = rn[g][1];
+    }
   }
 }
 
@@ -338,15 +431,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * MH * BN);
         uint32_t accumulate = 0;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          ok = waitBar(&sm->a_full[slot], a_phase, err, 14);
+          ok = mbarTryWait(&sm->a_full[slot], a_phase) || waitBar(&sm->a_full[slot], a_phase, err, 14);
           if (!ok) break;
           tcFenceAfter();
           const uint64_t a_base = a_desc0 + static_cast<uint64_t>(slot) * a_slot_units;
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
-            ok = waitBar(&sm->b_full[bs], b_phase, err, 15);
+            const uint2 offs = sm->a_off[st];  // read before the wait: it does not depend on the stage
+            ok = mbarTryWait(&sm->b_full[bs], b_phase) || waitBar(&sm->b_full[bs], b_phase, err, 15);
             if (!ok) break;
             tcFenceAfter();
-            const uint2 offs = sm->a_off[st];
             const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
 #pragma unroll
             for (int h = 0; h < MH; ++h) {
@@ -378,8 +471,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kSpan = MH == 1 ? BN / 2 : BN;  // columns converted by one warp
     const int m_half = MH == 1 ? 0 : pair;
     const int row_in_tile = m_half * kBlockM + quarter * 32 + lane;
-    const unsigned char* res = static_cast<const unsigned char*>(d.residual);
-    unsigned char* dst = static_cast<unsigned char*>(d.dst);
     uint32_t t_iter = 0;
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t_iter) {
       const int m0 = (tile / pl.n_tiles) * kTileM;
@@ -387,93 +478,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = static_cast<int>(t_iter % kBufs);
       if (!waitBar(&sm->acc_full[buf], (t_iter / kBufs) & 1, err, 17)) break;
       tcFenceAfter();
-      const int r = m0 + row_in_tile;
-      bool valid = r < d.rows;
-      long long drow = 0;
-      int ch_base = 0;
-      int pos_row = 0;
-      if (valid) {
-        const int img = r / d.img_rows;
-        const int loc = r - img * d.img_rows;
-        const int gy = loc / d.grid_w;
-        const int gx = loc - gy * d.grid_w;
-        valid = gy < d.valid_h && gx < d.valid_w;
-        switch (d.dst_mode) {
-          case FPK_DST_S2D:
-            drow = static_cast<long long>(img) * d.dst_img_rows + ((gy + 1) >> 1) * d.dst_grid_w +
-                   ((gx + 1) >> 1);
-            ch_base = (((gy + 1) & 1) * 2 + ((gx + 1) & 1)) * d.cout;
-            break;
-          case FPK_DST_CONCAT:
-            drow = static_cast<long long>(img % d.img_mod) * d.img_rows + loc;
-            ch_base = (img / d.img_mod) * d.ch_step;
-            break;
-          case FPK_DST_TOKENS:
-            drow = static_cast<long long>(img) * d.valid_h * d.valid_w + gy * d.valid_w + gx;
-            pos_row = gy * d.valid_w + gx;
-            break;
-          default:
-            drow = r;
-        }
-      }
-      const bool has_res = valid && res != nullptr;
-      const int j0 = MH == 1 ? pair * kSpan : 0;
-      // Residual rows of the next 32 columns are fetched while the current
-      // 32 are converted and stored.
-      uint4 rv[4][2] = {}, rn[4][2] = {};
-      if (has_res) {
-#pragma unroll
-        for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j0 + g * 8, r, rv[g]);
-      }
       const uint32_t t_base =
           tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
           static_cast<uint32_t>((buf * MH + m_half) * BN);
-#pragma unroll 1
-      for (int j = j0; j < j0 + kSpan; j += 32) {
-        uint32_t acc[32];
-        FPB_TMEM_LD32(t_base + j, acc);
-        if (has_res && j + 32 < j0 + kSpan) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j + 32 + g * 8, r, rn[g]);
-        }
-        tmemWaitLd();
-        if (valid) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int n = n0 + j + g * 8;
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[g * 8 + e]);
-            if (d.bias != nullptr) {
-              const float4 b0 = __ldg(reinterpret_cast<const float4*>(d.bias + n));
-              const float4 b1 = __ldg(reinterpret_cast<const float4*>(d.bias + n + 4));
-              v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
-              v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
-            }
-            if (has_res) {
-              float rf[8];
-              unpackRec8<T>(rv[g], rf);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] += rf[e];
-            }
-            if (d.relu) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = fmaxf(v[e], 0.0f);
-            }
-            if (d.dst_mode == FPK_DST_TOKENS && d.pos != nullptr) {
-              const float* pp = d.pos + static_cast<long long>(pos_row) * d.cout + n;
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
-            }
-            storeRec8<T>(dst, d.dst_plane_stride, ch_base + n, drow, v);
-          }
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          rv[g][0] = rn[g][0];
-          rv[g][1] = rn[g][1];
-        }
-      }
+      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, MH == 1 ? pair * kSpan : 0);
       tcFenceBefore();
       __syncwarp();
       if (lane == 0) mbarArrive(&sm->acc_empty[buf]);
@@ -484,6 +492,216 @@ __global__ void __launch_bounds__(kThreads, 1)
     tcFenceAfter();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols));
+  }
+}
+
+// CTA-pair variant (clusters of two CTAs, tcgen05 cta_group::2) for layers
+// with 256-channel tiles. A pair owns tiles of 256 rows x BN
+// channels: CTA r (r = 0 leader, 1 peer) stages the activation window of rows
+// m0 + 128 r and weight rows n0 + r BN/2 .. + BN/2 in its own shared memory,
+// and the leader's MMA lane issues M=256 x N=BN MMAs that read A from each CTA
+// and B half from each; accumulator rows 0-127 land in the leader's TMEM,
+// 128-255 in the peer's. Per SM this halves the weight bytes staged and read
+// per MMA, which is what limits the single-CTA 128 x 256 tile (shared-memory
+// bandwidth), and leaves room for two accumulator buffers at BN = 256.
+//   * both producers wait on their own `empty` barriers (the leader's commits
+//     signal both CTAs) and count their tile loads on the leader's `full`
+//     barriers, which the leader arms with the bytes of both CTAs;
+//   * both CTAs' epilogues wait on their own `acc_full` (signalled by the
+//     leader's commit) and release the buffer on the leader's `acc_empty`.
+// Activation windows are 3-D TMA tiles {16 B record, rows, planes} (zero fill
+// outside the tensor), so the window may not exceed 256 rows.
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemmPairKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w,
+                   const __grid_constant__ CUtensorMap tmap_a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* b_smem = base;
+  unsigned char* a_smem = b_smem + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes;
+  Smem* sm = reinterpret_cast<Smem*>(a_smem + static_cast<size_t>(pl.a_slots) * pl.a_slot_bytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = clusterCtaRank();
+  const bool leader = rank == 0;
+  int* err = d.error_flag;
+  constexpr uint32_t kTmemCols = 2 * BN;  // two accumulator buffers of 128 lanes x BN
+  constexpr int kPairM = 2 * kBlockM;
+  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+
+  if (threadIdx.x < pl.stages_per_chunk * 2) {
+    constexpr int kStep = 32 / Elem<T>::kBytes;
+    const uint32_t plane_units = static_cast<uint32_t>(pl.win_rows);
+    uint32_t packed = 0;
+    for (int h = 0; h < 2; ++h) {
+      const int k_local = (threadIdx.x * 2 + h) * kStep;
+      const int tap = k_local / pl.cw;
+      const int c = k_local - tap * pl.cw;
+      const uint32_t off = static_cast<uint32_t>(d.tap_off[tap] - pl.min_off) +
+                           static_cast<uint32_t>(c / Elem<T>::kPerRecord) * plane_units;
+      packed |= (off & 0xFFFFu) << (16 * h);
+    }
+    reinterpret_cast<uint32_t*>(sm->a_off)[threadIdx.x] = packed;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbarInit(&sm->acc_full[i], 1);
+      mbarInit(&sm->acc_empty[i], 2 * kEpilogueWarps);
+    }
+    for (int i = 0; i < pl.a_slots; ++i) {
+      mbarInit(&sm->a_full[i], 1);
+      mbarInit(&sm->a_empty[i], 1);
+    }
+    for (int i = 0; i < pl.b_stages; ++i) {
+      mbarInit(&sm->b_full[i], 1);
+      mbarInit(&sm->b_empty[i], 1);
+    }
+    mbarInit(&sm->drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smemU32(&sm->tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  __syncthreads();
+  tcFenceBefore();
+  // Both CTAs' barriers are initialised and both TMEM allocations made before
+  // any thread signals the peer or any MMA writes the peer's TMEM.
+  clusterSync();
+  tcFenceAfter();
+  const uint32_t tmem = sm->tmem_base;
+  const int n_tiles_total = pl.m_tiles * pl.n_tiles;
+  const int pair_id = static_cast<int>(blockIdx.x >> 1);
+  const int n_pairs = static_cast<int>(gridDim.x >> 1);
+  const int taps_cw = d.taps * pl.cw;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer (both CTAs) ----------------
+      int slot = 0, bs = 0;
+      uint32_t a_phase = 0, b_phase = 0, a_iter = 0, b_iter = 0;
+      bool ok = true;
+      const int row_off = static_cast<int>(rank) * kBlockM + pl.min_off;
+      const int n_off = static_cast<int>(rank) * (BN / 2);
+      for (int tile = pair_id; tile < n_tiles_total && ok; tile += n_pairs) {
+        const int m0 = (tile / pl.n_tiles) * kPairM;
+        const int n0 = (tile % pl.n_tiles) * BN;
+        for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
+          ok = waitBar(&sm->a_empty[slot], a_phase ^ 1, err, 21);
+          if (!ok) break;
+          if (leader) mbarExpectTx(&sm->a_full[slot], 2u * pl.a_win_bytes);
+          tmaLoad3dPair(a_smem + static_cast<size_t>(slot) * pl.a_slot_bytes, &tmap_a, 0, m0 + row_off,
+                        ch * pl.planes, mapaShared(smemU32(&sm->a_full[slot]), 0));
+          ++a_iter;
+          if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
+          for (int st = 0; st < pl.stages_per_chunk; ++st) {
+            ok = waitBar(&sm->b_empty[bs], b_phase ^ 1, err, 22);
+            if (!ok) break;
+            if (leader) mbarExpectTx(&sm->b_full[bs], 2u * pl.b_stage_bytes);
+            tmaLoad2dPair(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
+                          ch * taps_cw + st * Elem<T>::kPerStage, n0 + n_off,
+                          mapaShared(smemU32(&sm->b_full[bs]), 0));
+            ++b_iter;
+            if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
+          }
+        }
+      }
+      // Drain: the last use of every slot and stage must have been consumed by
+      // the leader's MMAs (which implies its loads landed) before the CTA exits.
+      const uint32_t na = static_cast<uint32_t>(pl.a_slots);
+      for (uint32_t i = a_iter > na ? a_iter - na : 0; i < a_iter; ++i) {
+        drainBar(&sm->a_empty[i % na], (i / na) & 1);
+      }
+      const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
+      for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
+        drainBar(&sm->b_empty[i % nb], (i / nb) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA) ----------------
+      const uint32_t idesc = Elem<T>::instrDesc(BN, kPairM);
+      const uint64_t a_desc0 =
+          smemDesc(smemU32(a_smem), static_cast<uint32_t>(pl.win_rows) * 16u, 128u, kLayoutNone);
+      const uint64_t b_desc0 = smemDesc(smemU32(b_smem), 16u, 1024u, kLayoutSw128);
+      const uint32_t a_slot_units = pl.a_slot_bytes >> 4;
+      const uint32_t b_stage_units = pl.b_stage_bytes >> 4;
+      int slot = 0, bs = 0;
+      uint32_t a_phase = 0, b_phase = 0, t_iter = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < n_tiles_total && ok; tile += n_pairs, ++t_iter) {
+        const int buf = static_cast<int>(t_iter & 1);
+        ok = waitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 23);
+        if (!ok) break;
+        tcFenceAfter();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
+        uint32_t accumulate = 0;
+        for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
+          ok = mbarTryWait(&sm->a_full[slot], a_phase) || waitBar(&sm->a_full[slot], a_phase, err, 24);
+          if (!ok) break;
+          tcFenceAfter();
+          const uint64_t a_base = a_desc0 + static_cast<uint64_t>(slot) * a_slot_units;
+          for (int st = 0; st < pl.stages_per_chunk; ++st) {
+            const uint2 offs = sm->a_off[st];  // read before the wait: it does not depend on the stage
+            ok = mbarTryWait(&sm->b_full[bs], b_phase) || waitBar(&sm->b_full[bs], b_phase, err, 25);
+            if (!ok) break;
+            tcFenceAfter();
+            const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
+            if constexpr (Elem<T>::kTf32) {
+              tcMmaPairTf32(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              tcMmaPairTf32(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
+              tcMmaPairTf32(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              tcMmaPairTf32(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+            } else {
+              tcMmaPairF16(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              tcMmaPairF16(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
+              tcMmaPairF16(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              tcMmaPairF16(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+            }
+            accumulate = 1u;
+            tcCommitPairBoth(&sm->b_empty[bs]);
+            if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
+          }
+          tcCommitPairBoth(&sm->a_empty[slot]);
+          if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
+        }
+        tcCommitPairBoth(&sm->acc_full[buf]);
+      }
+      tcCommitPairOwn(&sm->drain);
+      waitBar(&sm->drain, 0, err, 26);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // which half of the BN columns this warp converts
+    constexpr int kSpan = BN / 2;
+    const int row_in_tile = static_cast<int>(rank) * kBlockM + quarter * 32 + lane;
+    uint32_t t_iter = 0;
+    for (int tile = pair_id; tile < n_tiles_total; tile += n_pairs, ++t_iter) {
+      const int m0 = (tile / pl.n_tiles) * kPairM;
+      const int n0 = (tile % pl.n_tiles) * BN;
+      const int buf = static_cast<int>(t_iter & 1);
+      if (!waitBar(&sm->acc_full[buf], (t_iter >> 1) & 1, err, 27)) break;
+      tcFenceAfter();
+      const uint32_t t_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, half * kSpan);
+      tcFenceBefore();
+      __syncwarp();
+      if (lane == 0) mbarArriveCluster(mapaShared(smemU32(&sm->acc_empty[buf]), 0));
+    }
+  }
+  __syncthreads();
+  tcFenceBefore();
+  // Neither CTA frees its TMEM (or exits) while the leader's MMAs or the
+  // peer's signals may still touch it.
+  clusterSync();
+  if (warp == 1) {
+    tcFenceAfter();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
@@ -530,6 +748,52 @@ int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map
   return 0;
 }
 
+// 3-D map over a planar activation for the CTA-pair kernel: {16-byte record,
+// row, plane}; one box is a window of win_rows rows x `planes` planes, laid
+// out in shared memory exactly like the bulk-copied windows ([plane][row][16 B]).
+// Rows outside [0, rows) read as zeros (the guard rows of the layout are zero).
+int makeActivationMap(const fpk_gemm_desc_t& d, int total_planes, int win_rows, int planes, CUtensorMap* map) {
+  EncodeTiledFn enc = encodeFn();
+  if (enc == nullptr) return fail("fpk_gemm: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {16u, static_cast<cuuint64_t>(d.rows), static_cast<cuuint64_t>(total_planes)};
+  const cuuint64_t strides[2] = {16u, static_cast<cuuint64_t>(d.a_plane_stride)};
+  const cuuint32_t box[3] = {16u, static_cast<cuuint32_t>(win_rows), static_cast<cuuint32_t>(planes)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(d.a), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail("fpk_gemm: cuTensorMapEncodeTiled (activations) failed (" + std::to_string(r) + ")");
+  }
+  return 0;
+}
+
+// Splits the shared memory left after the barriers between activation window
+// slots and weight stages so that the MMAs can run furthest ahead of the
+// loads: the number of weight stages covered by both the window slots in
+// flight (slots x stages per window) and the weight stages themselves.
+// Convolutions (many stages per window) end up with two slots; 1x1 layers (one
+// stage per window) with as many slots as stages. Returns false if fewer than
+// two of each fit.
+bool chooseSlots(uint32_t slot_bytes, uint32_t stage_bytes, int stages_per_chunk, int* slots_out,
+                 int* stages_out) {
+  int best = -1;
+  for (int slots = 2; slots <= kMaxASlots; ++slots) {
+    const size_t used = 1024 + sizeof(Smem) + static_cast<size_t>(slots) * slot_bytes;
+    if (used >= kSmemBytes) break;
+    int stages = static_cast<int>((kSmemBytes - used) / stage_bytes);
+    stages = stages > kMaxBStages ? kMaxBStages : stages;
+    if (stages < 2) break;
+    const int depth = slots * stages_per_chunk < stages ? slots * stages_per_chunk : stages;
+    if (depth > best) {
+      best = depth;
+      *slots_out = slots;
+      *stages_out = stages;
+    }
+  }
+  return best > 0;
+}
+
 int numSms() {
   static int value = 0;
   if (value == 0) {
@@ -561,6 +825,63 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   prof::countLaunch(prof::kGemm);
   gemmKernel<T, BN, MH><<<grid, kThreads, smem, stream>>>(d, pl, map);
   return checkLaunch("gemmKernel");
+}
+
+bool g_cta_pairs = true;
+
+template <typename T, int BN>
+int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
+               size_t smem, cudaStream_t stream) {
+  static int attr_mask = 0;
+  static std::mutex mu;
+  static std::unordered_map<long long, int> clusters_for;  // (device, smem) -> co-resident pairs
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 31 && !(attr_mask & (1 << dev))) {
+    const cudaError_t e = cudaFuncSetAttribute(gemmPairKernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(std::string("fpk_gemm (pairs) smem attribute: ") + cudaGetErrorString(e));
+    }
+    attr_mask |= 1 << dev;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const long long key = (static_cast<long long>(dev) << 32) | static_cast<long long>(smem);
+    auto it = clusters_for.find(key);
+    if (it == clusters_for.end()) {
+      cfg.gridDim = dim3(2 * (numSms() / 2));
+      if (cudaOccupancyMaxActiveClusters(&clusters, gemmPairKernel<T, BN>, &cfg) != cudaSuccess || clusters < 1) {
+        cudaGetLastError();
+        clusters = numSms() / 2;
+      }
+      clusters_for.emplace(key, clusters);
+    } else {
+      clusters = it->second;
+    }
+  }
+  const int tiles = pl.m_tiles * pl.n_tiles;
+  cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
+  prof::countLaunch(prof::kGemm);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN>, d, pl, map_w, map_a);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(std::string("gemmPairKernel launch: ") + cudaGetErrorString(e));
+  }
+  return checkLaunch("gemmPairKernel");
 }
 
 template <typename T>
@@ -637,18 +958,66 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   auto plan = [&](int mh) {
     pl.win_rows = kBlockM * mh + (mx - mn);
     pl.a_win_bytes = static_cast<uint32_t>(pl.planes * pl.win_rows * 16);
-    int stages = 0;
-    for (int slots = pl.stages_per_chunk >= 4 ? 2 : kMaxASlots; slots >= 2; --slots) {
-      const size_t used = 1024 + sizeof(Smem) + static_cast<size_t>(slots) * pl.a_win_bytes;
-      stages = used < kSmemBytes ? static_cast<int>((kSmemBytes - used) / pl.b_stage_bytes) : 0;
-      pl.a_slots = slots;
-      if (stages >= 4 || slots == 2) break;
-    }
-    pl.b_stages = stages > kMaxBStages ? kMaxBStages : stages;
+    pl.a_slot_bytes = pl.a_win_bytes;
     pl.m_tiles = (d.rows + kBlockM * mh - 1) / (kBlockM * mh);
     pl.n_tiles = d.cout / bn;
-    return pl.b_stages >= 2;
+    return chooseSlots(pl.a_win_bytes, pl.b_stage_bytes, pl.stages_per_chunk, &pl.a_slots, &pl.b_stages);
   };
+  // CTA pairs (256-row tiles over two SMs) for 256-channel tiles whose
+  // activation window fits one TMA box, when there are pair tiles for every
+  // pair of SMs. (At 128 channels the single-CTA 256-row tiles are faster: an
+  // M=256 x N=128 pair MMA is too short to hide its issue cost.)
+  const int kprime = pl.n_chunks * d.taps * pl.cw;
+  auto s = static_cast<cudaStream_t>(stream);
+  // 1x1 layers without a residual stay on single-CTA 256 x 256 tiles (eight
+  // MMAs per weight stage); with a residual the pairs' second accumulator
+  // buffer, which overlaps the heavier epilogue with the next tile, wins.
+  const bool pair_shape = d.taps > 1 || d.residual != nullptr;
+  if (g_cta_pairs && bn == 256 && pair_shape && kBlockM + (mx - mn) <= 256) {
+    // For 1x1 layers the weight order does not depend on the chunk width
+    // (k' = channel), so wider windows (fewer activation barriers per MMA) are
+    // free to choose; the widest that keeps the pipeline as deep is taken.
+    Plan pp = pl;
+    pp.win_rows = kBlockM + (mx - mn);
+    pp.b_stage_bytes = static_cast<uint32_t>(bn / 2) * 128u;
+    pp.m_tiles = (d.rows + 2 * kBlockM - 1) / (2 * kBlockM);
+    pp.n_tiles = d.cout / bn;
+    bool planned = false;
+    int best_depth = 0;
+    for (int cw = pl.cw; cw <= (d.taps == 1 ? 4 * stage_elems : pl.cw) && cw <= d.cin; cw *= 2) {
+      if (d.cin % cw != 0) continue;
+      Plan c = pp;
+      c.cw = cw;
+      c.planes = cw * esize / 16;
+      c.n_chunks = d.cin / cw;
+      c.stages_per_chunk = d.taps * cw / stage_elems;
+      if (c.stages_per_chunk > kMaxStagesPerChunk) continue;
+      c.a_win_bytes = static_cast<uint32_t>(c.planes * c.win_rows * 16);
+      c.a_slot_bytes = (c.a_win_bytes + 1023u) & ~1023u;
+      if (!chooseSlots(c.a_slot_bytes, c.b_stage_bytes, c.stages_per_chunk, &c.a_slots, &c.b_stages)) continue;
+      const int depth = c.a_slots * c.stages_per_chunk < c.b_stages ? c.a_slots * c.stages_per_chunk : c.b_stages;
+      if (depth >= best_depth) {
+        best_depth = depth;
+        pp = c;
+        planned = true;
+      }
+    }
+    if (planned && pp.m_tiles * pp.n_tiles >= numSms() / 2) {
+      const size_t smem = 1024 + static_cast<size_t>(pp.b_stages) * pp.b_stage_bytes +
+                          static_cast<size_t>(pp.a_slots) * pp.a_slot_bytes + sizeof(Smem);
+      CUtensorMap map_w, map_a;
+      if (makeWeightMap(d, kprime, bn / 2, &map_w) != 0) return 1;
+      if (makeActivationMap(d, d.cin * esize / 16, pp.win_rows, pp.planes, &map_a) != 0) return 1;
+      switch (d.dtype) {
+        case FPK_DTYPE_BF16:
+          return launchPair<__nv_bfloat16, 256>(d, pp, map_w, map_a, smem, s);
+        case FPK_DTYPE_F32:
+          return launchPair<float, 256>(d, pp, map_w, map_a, smem, s);
+        default:
+          return launchPair<__half, 256>(d, pp, map_w, map_a, smem, s);
+      }
+    }
+  }
   // Narrow layers (BN <= 128) take 256-row tiles when there are enough rows
   // to keep every SM busy.
   int mh = 1;
@@ -664,10 +1033,8 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   }
   const size_t smem = 1024 + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes +
                       static_cast<size_t>(pl.a_slots) * pl.a_win_bytes + sizeof(Smem);
-  const int kprime = pl.n_chunks * d.taps * pl.cw;
   CUtensorMap map;
   if (makeWeightMap(d, kprime, bn, &map) != 0) return 1;
-  auto s = static_cast<cudaStream_t>(stream);
   switch (d.dtype) {
     case FPK_DTYPE_BF16:
       return launchShape<__nv_bfloat16>(d, pl, map, smem, s, bn, mh);
@@ -676,4 +1043,10 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     default:
       return launchShape<__half>(d, pl, map, smem, s, bn, mh);
   }
+}
+
+extern "C" int fpk_gemm_set_cta_pairs(int enable) {
+  const int prev = fpb::gemm::g_cta_pairs ? 1 : 0;
+  fpb::gemm::g_cta_pairs = enable != 0;
+  return prev;
 }

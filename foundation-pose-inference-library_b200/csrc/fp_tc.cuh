@@ -87,6 +87,94 @@ __device__ __forceinline__ void tmaLoad2d(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
+// ---- CTA pairs (clusters of two CTAs driving one cta_group::2 MMA) ----
+
+__device__ __forceinline__ uint32_t clusterCtaRank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapaShared(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+// Every thread of both CTAs: release this CTA's prior writes, wait for the peer.
+__device__ __forceinline__ void clusterSync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (possibly the peer CTA's).
+__device__ __forceinline__ void mbarArriveCluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// Tiled loads for a CTA pair: the data lands in this CTA's shared memory, the
+// transaction bytes are counted on the mbarrier at `bar_cluster` (the pair
+// leader's), so one barrier tracks both halves of an MMA operand.
+__device__ __forceinline__ void tmaLoad2dPair(void* dst, const CUtensorMap* map, int c0, int c1,
+                                              uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4}], [%2];" ::"r"(smemU32(dst)),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmaLoad3dPair(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                              uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4, %5}], [%2];" ::"r"(smemU32(dst)),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Pair MMA, issued by the leader CTA only: D rows 0-127 live in the leader's
+// TMEM, rows 128-255 in the peer's; A rows come from each CTA's own shared
+// memory and B columns half from each, at the same offsets.
+__device__ __forceinline__ void tcMmaPairF16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tcMmaPairTf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Completion of the leader's prior pair MMAs signalled on the mbarrier at the
+// same offset in both CTAs of the pair (cta_mask 0b11).
+__device__ __forceinline__ void tcCommitPairBoth(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smemU32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// Completion of the leader's prior pair MMAs signalled on its own mbarrier.
+__device__ __forceinline__ void tcCommitPairOwn(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smemU32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void tcFenceBefore() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

@@ -59,6 +59,7 @@ def bench_gemm(args) -> dict:
     from fp_b200.kernels import FPK_DST_SAME, FPK_DTYPE_BF16, FPK_DTYPE_F16, FpkLibrary, GemmDesc, gemm
 
     fpk = FpkLibrary()
+    fpk.lib.fpk_gemm_set_cta_pairs(args.pairs)
     dt = torch.float16 if args.dtype == "f16" else torch.bfloat16
     g = args.grid
     valid = g - 1
@@ -80,7 +81,7 @@ def bench_gemm(args) -> dict:
     d.img_mod, d.dtype, d.error_flag = 1, FPK_DTYPE_F16 if args.dtype == "f16" else FPK_DTYPE_BF16, err.data_ptr()
     ms = time_fn(torch, lambda: gemm(fpk, d), args.iters)
     flops = 2.0 * args.batch * valid * valid * args.cout * len(taps) * args.cin
-    return {"kernel": "gemmKernel", "batch": args.batch, "cin": args.cin, "cout": args.cout,
+    return {"kernel": "gemmKernel", "cta_pairs": args.pairs, "batch": args.batch, "cin": args.cin, "cout": args.cout,
             "grid": g, "taps": len(taps), "ms": ms, "tflops": flops / ms / 1e9,
             "hbm_bytes": (rows * (args.cin + args.cout)) * 2, "error_flag": int(err.item())}
 
@@ -161,6 +162,8 @@ def main() -> None:
     ap.add_argument("--faces", type=int, default=50000)
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--pairs", type=int, default=1, choices=[0, 1],
+                    help="gemm: allow CTA-pair (cta_group::2) tiles (1, default) or single-CTA tiles only (0)")
     args = ap.parse_args()
     fn = {"gemm": bench_gemm, "render": bench_render, "attention": bench_attention}[args.what]
     print(json.dumps(fn(args)), flush=True)

@@ -208,6 +208,13 @@ typedef struct fpk_gemm_desc {
 
 FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
 
+/* Convolutions and residual 1x1 layers with 256-channel output tiles (cout a
+ * multiple of 256) run as CTA pairs (clusters of two CTAs issuing tcgen05
+ * cta_group::2 MMAs on 256-row tiles) when their rows fill every SM;
+ * enable = 0 keeps every layer on single-CTA tiles. Process-wide;
+ * returns the previous setting. No reference counterpart (a tuning switch). */
+FP_API int fpk_gemm_set_cta_pairs(int enable);
+
 /* Fused multi-head self-attention on tcgen05/TMEM (head dim 128):
  * out = softmax(Q K^T / sqrt(128)) V for every (layer, head, sequence), over
  * planar activations of `dtype` (fp16/bf16 KP8, or fp32 KP4 run as TF32).
@@ -226,7 +233,7 @@ FP_API int fpk_attention(const void* qkv, long long qkv_plane_stride, int qkv_la
  * RefineNet / ScoreNet as a unit: the built-in inference backend behind
  * IInferenceRunner (reference include/foundation_pose_nvidia/inference_runner.hpp:12-30,
  * src/tensorrt_runner.cu:498-532). Weight packs (.fpw) replace the ONNX files;
- * precision is FP_PRECISION_FP16 or FP_PRECISION_BF16 in this build.
+ * precision is any FP_PRECISION_* (FP32 and TF32 both run as TF32 on the tensor cores).
  * Inputs are NCHW [n,6,160,160] fp32 device tensors (rendered = inputA,
  * observed = inputB); outputs are device fp32 trans/rot [n,3] and score [n].
  * A handle owns its device memory for max_batch hypotheses on the current device. */

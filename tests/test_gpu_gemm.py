@@ -64,6 +64,17 @@ def err():
     return torch.zeros(1, dtype=torch.int32, device=DEV)
 
 
+@pytest.fixture(params=[1, 0], ids=["pairs", "single"])
+def cta_pairs(request, fpk):
+    """Runs a test with CTA-pair tiles allowed (the default; layers of 128/256
+    output channels per tile with rows for every SM pair take them) and with
+    every layer on single-CTA tiles. Pair tiles need 256-channel tiles and
+    rows for every pair of SMs."""
+    prev = fpk.lib.fpk_gemm_set_cta_pairs(request.param)
+    yield request.param
+    fpk.lib.fpk_gemm_set_cta_pairs(prev)
+
+
 @pytest.mark.parametrize("m,cin,cout,dtype", [(1000, 64, 64, FPK_DTYPE_BF16),
                                               (777, 128, 128, FPK_DTYPE_F16),
                                               (2000, 256, 256, FPK_DTYPE_BF16),
@@ -74,8 +85,12 @@ def err():
                                               # > 2 x 148 tiles of 128 rows: 256-row tiles with
                                               # one accumulator buffer for 1x1 layers
                                               (40000, 512, 768, FPK_DTYPE_F16),
-                                              (40000, 256, 512, FPK_DTYPE_F32)])
-def test_plain_gemm(fpk, err, m, cin, cout, dtype):
+                                              (40000, 256, 512, FPK_DTYPE_F32),
+                                              # pair tiles in BF16 with a ragged last pair
+                                              # tile; 128-wide windows of a 1x1 layer
+                                              (37001, 256, 256, FPK_DTYPE_BF16),
+                                              (20111, 512, 1536, FPK_DTYPE_BF16)])
+def test_plain_gemm(fpk, err, cta_pairs, m, cin, cout, dtype):
     g = torch.Generator().manual_seed(m + cin)
     dt = DT[dtype]
     A = torch.randn(m, cin, generator=g)
@@ -103,8 +118,12 @@ def test_plain_gemm(fpk, err, m, cin, cout, dtype):
                                                  (256, 256, 40, FPK_DTYPE_BF16, 3),
                                                  (128, 128, 40, FPK_DTYPE_F32, 24),
                                                  (256, 256, 40, FPK_DTYPE_F32, 3),
-                                                 (512, 512, 20, FPK_DTYPE_BF16, 3)])
-def test_conv3x3_residual_relu(fpk, err, cin, cout, hw, dtype, n):
+                                                 (512, 512, 20, FPK_DTYPE_BF16, 3),
+                                                 # enough rows for pair tiles at 256 channels
+                                                 (256, 256, 40, FPK_DTYPE_F16, 25),
+                                                 (512, 512, 20, FPK_DTYPE_BF16, 64),
+                                                 (256, 256, 40, FPK_DTYPE_F32, 25)])
+def test_conv3x3_residual_relu(fpk, err, cta_pairs, cin, cout, hw, dtype, n):
     g = torch.Generator().manual_seed(cin * 7 + hw + n)
     dt = DT[dtype]
     H, W = hw, hw
@@ -227,10 +246,11 @@ def test_stem_7x7_stride2(fpk, err, dtype, n):
     close(got, ref.permute(0, 2, 3, 1))
 
 
-def test_tokens_epilogue(fpk, err):
+@pytest.mark.parametrize("n", [3, 200])
+def test_tokens_epilogue(fpk, err, cta_pairs, n):
     g = torch.Generator().manual_seed(3)
     dt = torch.bfloat16
-    n, H, cin, cout = 3, 20, 128, 256
+    H, cin, cout = 20, 128, 256
     gw = H + 1
     rows = n * (H + 1) * gw
     X = torch.randn(n, H, H, cin, generator=g)
@@ -249,3 +269,36 @@ def test_tokens_epilogue(fpk, err):
     ref = torch.relu(X.reshape(n, H * H, cin).to(dt).float().to(DEV) @ Wt.to(dt).float().to(DEV).T)
     ref = ref + pos[None]
     close(out.get().reshape(n, H * H, cout), ref)
+
+
+@pytest.mark.parametrize("dtype,cout", [(FPK_DTYPE_F16, 256), (FPK_DTYPE_BF16, 512), (FPK_DTYPE_F32, 256)])
+def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout):
+    """A 3x3 conv with enough rows for pair tiles gives the same bits on CTA
+    pairs (M=256 cta_group::2 MMAs) as on single-CTA tiles: both accumulate
+    every output over the same K sequence in fp32."""
+    g = torch.Generator().manual_seed(11)
+    dt = DT[dtype]
+    n, H, cin = 30, 40, 256
+    gw = H + 1
+    img_rows = (H + 1) * gw
+    rows = n * img_rows
+    z = torch.zeros(n, H + 1, gw, cin)
+    z[:, :H, :H] = torch.randn(n, H, H, cin, generator=g)
+    Wt = torch.randn(cout, 9, cin, generator=g) / math.sqrt(9 * cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+    pa = Planar(rows, cin, dt).set(z.reshape(rows, cin).to(DEV))
+    w = chunk_major(Wt, dtype).to(dt).to(DEV)
+    taps = [(ky - 1) * gw + (kx - 1) for ky in range(3) for kx in range(3)]
+    outs = []
+    for pairs in (1, 0):
+        prev = fpk.lib.fpk_gemm_set_cta_pairs(pairs)
+        try:
+            out = Planar(rows, cout, dt)
+            gemm(fpk, make_desc(pa, rows, cin, taps, w, cout, out, dtype, err, bias=b, relu=True,
+                                img_rows=img_rows, grid_w=gw, valid_h=H, valid_w=H))
+            torch.cuda.synchronize()
+        finally:
+            fpk.lib.fpk_gemm_set_cta_pairs(prev)
+        assert err.item() == 0
+        outs.append(out.get())
+    assert torch.equal(outs[0], outs[1])
