@@ -1,14 +1,21 @@
 // Persistent tcgen05 implicit-GEMM kernel (sm_100a) for RefineNet / ScoreNet.
 //
 // One CTA per SM walks output tiles of 128 (or, for layers of at most 128
-// output channels, 256) rows x BN channels. Warp roles:
+// output channels, 256) rows x BN channels; convolutions and residual 1x1
+// layers of 256-channel tiles run on CTA pairs instead (gemmPairKernel below).
+// Warp roles:
 //   warp 0     producer: per 64-channel chunk, one bulk copy per channel plane
 //              brings a window of 128 + span rows of the activation into shared
 //              memory (reused by every tap of the convolution); per 64-wide K
 //              stage a TMA tile load brings the weights (128B swizzle).
-//   warp 1     MMA issuer (one lane) + TMEM owner: tcgen05.mma kind::f16,
-//              M=128, N=BN, K=16, fp32 accumulators in TMEM, two accumulator
-//              buffers so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   warp 1     MMA issuer + TMEM owner: tcgen05.mma kind::f16 (kind::tf32
+//              for fp32), M=128, N=BN, K=16, fp32 accumulators in TMEM, two
+//              accumulator buffers so the epilogue of tile i overlaps the MMAs
+//              of tile i+1. The whole warp runs the issue loop, so descriptors
+//              and loop state stay warp-uniform, and an elected lane issues
+//              each instruction: the issue rate, not the tensor core, bounds
+//              the narrow (N <= 128) layers, and a single-lane loop issued
+//              measurably slower.
 //   warps 2-9  epilogue, two warps per TMEM lane quarter (each converts half
 //              of the BN columns, or with 256-row tiles one 128-row half):
 //              tcgen05.ld rows of the accumulator, bias /
@@ -94,6 +101,16 @@ __device__ __forceinline__ void mmaT(uint32_t d_tmem, uint64_t a_desc, uint64_t 
         : "memory");
   } else {
     tcMma(d_tmem, a_desc, b_desc, idesc, accumulate);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void mmaTElect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  if constexpr (Elem<T>::kTf32) {
+    tcMmaTf32Elect(d_tmem, a_desc, b_desc, idesc, accumulate);
+  } else {
+    tcMmaElect(d_tmem, a_desc, b_desc, idesc, accumulate);
   }
 }
 
@@ -409,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ---------------- MMA issuer ----------------
       // Descriptors are built once; per K=16 step only the 14-bit start
       // address field changes (an add that cannot carry: every start is a
@@ -425,19 +442,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++t_iter) {
         const int buf = static_cast<int>(t_iter % kBufs);
-        ok = waitBar(&sm->acc_empty[buf], ((t_iter / kBufs) & 1) ^ 1, err, 13);
+        ok = warpWaitBar(&sm->acc_empty[buf], ((t_iter / kBufs) & 1) ^ 1, err, 13);
         if (!ok) break;
         tcFenceAfter();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * MH * BN);
         uint32_t accumulate = 0;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          ok = mbarTryWait(&sm->a_full[slot], a_phase) || waitBar(&sm->a_full[slot], a_phase, err, 14);
+          ok = warpWaitBar(&sm->a_full[slot], a_phase, err, 14);
           if (!ok) break;
           tcFenceAfter();
           const uint64_t a_base = a_desc0 + static_cast<uint64_t>(slot) * a_slot_units;
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
             const uint2 offs = sm->a_off[st];  // read before the wait: it does not depend on the stage
-            ok = mbarTryWait(&sm->b_full[bs], b_phase) || waitBar(&sm->b_full[bs], b_phase, err, 15);
+            ok = warpWaitBar(&sm->b_full[bs], b_phase, err, 15);
             if (!ok) break;
             tcFenceAfter();
             const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
@@ -446,22 +463,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               // Half h reads the window 128 rows (128 x 16 B = 128 units) further on.
               const uint64_t ah = a_base + static_cast<uint64_t>(h * 128);
               const uint32_t dh = d_tmem + static_cast<uint32_t>(h * BN);
-              mmaT<T>(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-              mmaT<T>(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
-              mmaT<T>(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-              mmaT<T>(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
+              mmaTElect<T>(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              mmaTElect<T>(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
+              mmaTElect<T>(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              mmaTElect<T>(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
             }
             accumulate = 1u;
-            tcCommit(&sm->b_empty[bs]);
+            tcCommitElect(&sm->b_empty[bs]);
             if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
-          tcCommit(&sm->a_empty[slot]);
+          tcCommitElect(&sm->a_empty[slot]);
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
         }
-        tcCommit(&sm->acc_full[buf]);
+        tcCommitElect(&sm->acc_full[buf]);
       }
       // Drain: wait until every MMA issued above has completed.
-      tcCommit(&sm->drain);
+      tcCommitElect(&sm->drain);
       waitBar(&sm->drain, 0, err, 16);
     }
   } else {
@@ -622,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
+    if (leader) {
       // ---------------- MMA issuer (leader CTA) ----------------
       const uint32_t idesc = Elem<T>::instrDesc(BN, kPairM);
       const uint64_t a_desc0 =
@@ -635,43 +652,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = pair_id; tile < n_tiles_total && ok; tile += n_pairs, ++t_iter) {
         const int buf = static_cast<int>(t_iter & 1);
-        ok = waitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 23);
+        ok = warpWaitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 23);
         if (!ok) break;
         tcFenceAfter();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
         uint32_t accumulate = 0;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          ok = mbarTryWait(&sm->a_full[slot], a_phase) || waitBar(&sm->a_full[slot], a_phase, err, 24);
+          ok = warpWaitBar(&sm->a_full[slot], a_phase, err, 24);
           if (!ok) break;
           tcFenceAfter();
           const uint64_t a_base = a_desc0 + static_cast<uint64_t>(slot) * a_slot_units;
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
             const uint2 offs = sm->a_off[st];  // read before the wait: it does not depend on the stage
-            ok = mbarTryWait(&sm->b_full[bs], b_phase) || waitBar(&sm->b_full[bs], b_phase, err, 25);
+            ok = warpWaitBar(&sm->b_full[bs], b_phase, err, 25);
             if (!ok) break;
             tcFenceAfter();
             const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
             if constexpr (Elem<T>::kTf32) {
-              tcMmaPairTf32(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-              tcMmaPairTf32(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
-              tcMmaPairTf32(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-              tcMmaPairTf32(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+              tcMmaPairTf32Elect(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              tcMmaPairTf32Elect(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
+              tcMmaPairTf32Elect(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              tcMmaPairTf32Elect(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
             } else {
-              tcMmaPairF16(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-              tcMmaPairF16(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
-              tcMmaPairF16(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-              tcMmaPairF16(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+              tcMmaPairF16Elect(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+              tcMmaPairF16Elect(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
+              tcMmaPairF16Elect(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+              tcMmaPairF16Elect(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
             }
             accumulate = 1u;
-            tcCommitPairBoth(&sm->b_empty[bs]);
+            tcCommitPairBothElect(&sm->b_empty[bs]);
             if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
-          tcCommitPairBoth(&sm->a_empty[slot]);
+          tcCommitPairBothElect(&sm->a_empty[slot]);
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
         }
-        tcCommitPairBoth(&sm->acc_full[buf]);
+        tcCommitPairBothElect(&sm->acc_full[buf]);
       }
-      tcCommitPairOwn(&sm->drain);
+      tcCommitPairOwnElect(&sm->drain);
       waitBar(&sm->drain, 0, err, 26);
     }
   } else {
@@ -828,7 +845,6 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
 }
 
 bool g_cta_pairs = true;
-
 template <typename T, int BN>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
                size_t smem, cudaStream_t stream) {

@@ -66,10 +66,9 @@ def err():
 
 @pytest.fixture(params=[1, 0], ids=["pairs", "single"])
 def cta_pairs(request, fpk):
-    """Runs a test with CTA-pair tiles allowed (the default; layers of 128/256
-    output channels per tile with rows for every SM pair take them) and with
-    every layer on single-CTA tiles. Pair tiles need 256-channel tiles and
-    rows for every pair of SMs."""
+    """Runs a test with CTA-pair tiles allowed (the default: convolutions and
+    residual 1x1 layers with 256-channel tiles take them when their rows fill
+    every pair of SMs) and with every layer on single-CTA tiles."""
     prev = fpk.lib.fpk_gemm_set_cta_pairs(request.param)
     yield request.param
     fpk.lib.fpk_gemm_set_cta_pairs(prev)
@@ -89,6 +88,9 @@ def cta_pairs(request, fpk):
                                               # pair tiles in BF16 with a ragged last pair
                                               # tile; 128-wide windows of a 1x1 layer
                                               (37001, 256, 256, FPK_DTYPE_BF16),
+                                              # 128-channel layers on 256-row tiles
+                                              (40000, 256, 128, FPK_DTYPE_F16),
+                                              (38000, 128, 128, FPK_DTYPE_F32),
                                               (20111, 512, 1536, FPK_DTYPE_BF16)])
 def test_plain_gemm(fpk, err, cta_pairs, m, cin, cout, dtype):
     g = torch.Generator().manual_seed(m + cin)
@@ -271,14 +273,15 @@ def test_tokens_epilogue(fpk, err, cta_pairs, n):
     close(out.get().reshape(n, H * H, cout), ref)
 
 
-@pytest.mark.parametrize("dtype,cout", [(FPK_DTYPE_F16, 256), (FPK_DTYPE_BF16, 512), (FPK_DTYPE_F32, 256)])
-def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout):
+@pytest.mark.parametrize("dtype,cout,cin", [(FPK_DTYPE_F16, 256, 256), (FPK_DTYPE_BF16, 512, 256),
+                                            (FPK_DTYPE_F32, 256, 256)])
+def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout, cin):
     """A 3x3 conv with enough rows for pair tiles gives the same bits on CTA
     pairs (M=256 cta_group::2 MMAs) as on single-CTA tiles: both accumulate
     every output over the same K sequence in fp32."""
     g = torch.Generator().manual_seed(11)
     dt = DT[dtype]
-    n, H, cin = 30, 40, 256
+    n, H = 30, 40
     gw = H + 1
     img_rows = (H + 1) * gw
     rows = n * img_rows
@@ -290,12 +293,13 @@ def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout):
     w = chunk_major(Wt, dtype).to(dt).to(DEV)
     taps = [(ky - 1) * gw + (kx - 1) for ky in range(3) for kx in range(3)]
     outs = []
+    pr = Planar(rows, cout, dt).set(torch.randn(rows, cout, generator=g).to(DEV))
     for pairs in (1, 0):
         prev = fpk.lib.fpk_gemm_set_cta_pairs(pairs)
         try:
             out = Planar(rows, cout, dt)
-            gemm(fpk, make_desc(pa, rows, cin, taps, w, cout, out, dtype, err, bias=b, relu=True,
-                                img_rows=img_rows, grid_w=gw, valid_h=H, valid_w=H))
+            gemm(fpk, make_desc(pa, rows, cin, taps, w, cout, out, dtype, err, bias=b, residual=pr,
+                                relu=True, img_rows=img_rows, grid_w=gw, valid_h=H, valid_w=H))
             torch.cuda.synchronize()
         finally:
             fpk.lib.fpk_gemm_set_cta_pairs(prev)
