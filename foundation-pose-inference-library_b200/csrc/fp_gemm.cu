@@ -380,8 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int taps_cw = d.taps * pl.cw;
 
   if (warp == 0) {
-    if (lane == 0) {
+    {
       // ---------------- producer ----------------
+      // The whole warp runs the loop; lane p issues the bulk copy of channel
+      // plane p of each window, lane 0 arms the barriers and loads weights.
       const unsigned char* a_bytes = static_cast<const unsigned char*>(d.a);
       const uint32_t plane_bytes = static_cast<uint32_t>(pl.win_rows) * 16u;
       uint32_t a_iter = 0, b_iter = 0;
@@ -392,37 +394,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = (tile / pl.n_tiles) * kTileM;
         const int n0 = (tile % pl.n_tiles) * BN;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          ok = waitBar(&sm->a_empty[slot], a_phase ^ 1, err, 11);
+          ok = warpWaitBar(&sm->a_empty[slot], a_phase ^ 1, err, 11);
           if (!ok) break;
-          mbarExpectTx(&sm->a_full[slot], pl.a_win_bytes);
+          if (lane == 0) mbarExpectTx(&sm->a_full[slot], pl.a_win_bytes);
+          __syncwarp();
           unsigned char* win = a_smem + static_cast<size_t>(slot) * pl.a_win_bytes;
           const unsigned char* src = a_bytes + static_cast<long long>(ch * pl.planes) * d.a_plane_stride +
                                      static_cast<long long>(m0 + pl.min_off) * 16;
-          for (int p = 0; p < pl.planes; ++p) {
-            bulkCopy(win + p * plane_bytes, src, plane_bytes, &sm->a_full[slot]);
-            src += d.a_plane_stride;
+          for (int p = lane; p < pl.planes; p += 32) {
+            bulkCopy(win + p * plane_bytes, src + static_cast<long long>(p) * d.a_plane_stride, plane_bytes,
+                     &sm->a_full[slot]);
           }
           ++a_iter;
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
-            ok = waitBar(&sm->b_empty[bs], b_phase ^ 1, err, 12);
+            ok = warpWaitBar(&sm->b_empty[bs], b_phase ^ 1, err, 12);
             if (!ok) break;
-            mbarExpectTx(&sm->b_full[bs], pl.b_stage_bytes);
-            tmaLoad2d(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
-                      ch * taps_cw + st * Elem<T>::kPerStage, n0, &sm->b_full[bs]);
+            if (lane == 0) {
+              mbarExpectTx(&sm->b_full[bs], pl.b_stage_bytes);
+              tmaLoad2d(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
+                        ch * taps_cw + st * Elem<T>::kPerStage, n0, &sm->b_full[bs]);
+            }
             ++b_iter;
             if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
         }
       }
       // Drain: every load armed above must land before the CTA may exit.
-      const uint32_t na = static_cast<uint32_t>(pl.a_slots);
-      for (uint32_t i = a_iter > na ? a_iter - na : 0; i < a_iter; ++i) {
-        drainBar(&sm->a_full[i % na], (i / na) & 1);
-      }
-      const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
-      for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
-        drainBar(&sm->b_full[i % nb], (i / nb) & 1);
+      if (lane == 0) {
+        const uint32_t na = static_cast<uint32_t>(pl.a_slots);
+        for (uint32_t i = a_iter > na ? a_iter - na : 0; i < a_iter; ++i) {
+          drainBar(&sm->a_full[i % na], (i / na) & 1);
+        }
+        const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
+        for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
+          drainBar(&sm->b_full[i % nb], (i / nb) & 1);
+        }
       }
     }
   } else if (warp == 1) {
@@ -597,8 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int taps_cw = d.taps * pl.cw;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- producer (both CTAs) ----------------
+    {
+      // ---------------- producer (both CTAs; whole warp, lane 0 issues) ----------------
       int slot = 0, bs = 0;
       uint32_t a_phase = 0, b_phase = 0, a_iter = 0, b_iter = 0;
       bool ok = true;
@@ -608,20 +615,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = (tile / pl.n_tiles) * kPairM;
         const int n0 = (tile % pl.n_tiles) * BN;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
-          ok = waitBar(&sm->a_empty[slot], a_phase ^ 1, err, 21);
+          ok = warpWaitBar(&sm->a_empty[slot], a_phase ^ 1, err, 21);
           if (!ok) break;
-          if (leader) mbarExpectTx(&sm->a_full[slot], 2u * pl.a_win_bytes);
-          tmaLoad3dPair(a_smem + static_cast<size_t>(slot) * pl.a_slot_bytes, &tmap_a, 0, m0 + row_off,
-                        ch * pl.planes, mapaShared(smemU32(&sm->a_full[slot]), 0));
+          if (lane == 0) {
+            if (leader) mbarExpectTx(&sm->a_full[slot], 2u * pl.a_win_bytes);
+            tmaLoad3dPair(a_smem + static_cast<size_t>(slot) * pl.a_slot_bytes, &tmap_a, 0, m0 + row_off,
+                          ch * pl.planes, mapaShared(smemU32(&sm->a_full[slot]), 0));
+          }
           ++a_iter;
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
           for (int st = 0; st < pl.stages_per_chunk; ++st) {
-            ok = waitBar(&sm->b_empty[bs], b_phase ^ 1, err, 22);
+            ok = warpWaitBar(&sm->b_empty[bs], b_phase ^ 1, err, 22);
             if (!ok) break;
-            if (leader) mbarExpectTx(&sm->b_full[bs], 2u * pl.b_stage_bytes);
-            tmaLoad2dPair(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
-                          ch * taps_cw + st * Elem<T>::kPerStage, n0 + n_off,
-                          mapaShared(smemU32(&sm->b_full[bs]), 0));
+            if (lane == 0) {
+              if (leader) mbarExpectTx(&sm->b_full[bs], 2u * pl.b_stage_bytes);
+              tmaLoad2dPair(b_smem + static_cast<size_t>(bs) * pl.b_stage_bytes, &tmap_w,
+                            ch * taps_cw + st * Elem<T>::kPerStage, n0 + n_off,
+                            mapaShared(smemU32(&sm->b_full[bs]), 0));
+            }
             ++b_iter;
             if (++bs == pl.b_stages) { bs = 0; b_phase ^= 1; }
           }
@@ -629,13 +640,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: the last use of every slot and stage must have been consumed by
       // the leader's MMAs (which implies its loads landed) before the CTA exits.
-      const uint32_t na = static_cast<uint32_t>(pl.a_slots);
-      for (uint32_t i = a_iter > na ? a_iter - na : 0; i < a_iter; ++i) {
-        drainBar(&sm->a_empty[i % na], (i / na) & 1);
-      }
-      const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
-      for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
-        drainBar(&sm->b_empty[i % nb], (i / nb) & 1);
+      if (lane == 0) {
+        const uint32_t na = static_cast<uint32_t>(pl.a_slots);
+        for (uint32_t i = a_iter > na ? a_iter - na : 0; i < a_iter; ++i) {
+          drainBar(&sm->a_empty[i % na], (i / na) & 1);
+        }
+        const uint32_t nb = static_cast<uint32_t>(pl.b_stages);
+        for (uint32_t i = b_iter > nb ? b_iter - nb : 0; i < b_iter; ++i) {
+          drainBar(&sm->b_empty[i % nb], (i / nb) & 1);
+        }
       }
     }
   } else if (warp == 1) {
