@@ -98,29 +98,22 @@ __host__ __device__ constexpr uint32_t idesc(uint32_t fmt, int n, bool b_mn_majo
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kRows >> 4) << 24);
 }
 
+// MMAs issued by one elected lane of the (converged) issuing warp.
 template <typename T>
 __device__ __forceinline__ void mmaSS(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
   if constexpr (Geo<T>::kTf32) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(id), "r"(acc)
-        : "memory");
+    tcMmaTf32Elect(d, a, b, id, acc);
   } else {
-    tcMma(d, a, b, id, acc);
+    tcMmaElect(d, a, b, id, acc);
   }
 }
 
 template <typename T>
 __device__ __forceinline__ void mmaTS(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
   if constexpr (Geo<T>::kTf32) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-        "r"(a_tmem), "l"(b), "r"(id), "r"(acc)
-        : "memory");
+    tcMmaTf32TmemAElect(d, a_tmem, b, id, acc);
   } else {
-    tcMmaTmemA(d, a_tmem, b, id, acc);
+    tcMmaTmemAElect(d, a_tmem, b, id, acc);
   }
 }
 
@@ -258,20 +251,22 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ---------------- MMA issuer ----------------
+      // The whole warp runs the loop (warp-uniform descriptors); an elected
+      // lane issues each tcgen05 instruction.
       // PV: V as an MN-major B operand (16-bit), or the transposed K-major tile (fp32).
       const uint32_t idesc_o = idesc(G::fmt(), kHeadDim, !G::kTf32);
       const uint32_t q_addr = smemU32(q_s);
       const uint32_t k_addr = smemU32(k_s);
       const uint32_t v_addr = smemU32(v_s);
-      bool ok = waitBar(&bars->q_full, 0, err, 23);
+      bool ok = warpWaitBar(&bars->q_full, 0, err, 23);
       tcFenceAfter();
       for (int b = 0; b <= n_blocks && ok; ++b) {
         if (b < n_blocks) {
           const int slot = b & 1;
-          ok = waitBar(&bars->k_full[slot], (b >> 1) & 1, err, 24);
-          if (ok && b >= 2) ok = waitBar(&bars->s_free[slot], ((b >> 1) - 1) & 1, err, 25);
+          ok = warpWaitBar(&bars->k_full[slot], (b >> 1) & 1, err, 24);
+          if (ok && b >= 2) ok = warpWaitBar(&bars->s_free[slot], ((b >> 1) - 1) & 1, err, 25);
           if (!ok) break;
           tcFenceAfter();
           const int keys = min(kKeys, a.seq_len - b * kKeys);
@@ -286,16 +281,16 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
                                          128, kLayoutNone);
             mmaSS<T>(d, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
           }
-          tcCommit(&bars->s_full[slot]);
-          tcCommit(&bars->k_empty[slot]);
+          tcCommitElect(&bars->s_full[slot]);
+          tcCommitElect(&bars->k_empty[slot]);
         }
         if (b >= 1) {
           const int j = b - 1;
           const int slot = j & 1;
-          ok = waitBar(&bars->p_full, j & 1, err, 26);
+          ok = warpWaitBar(&bars->p_full, j & 1, err, 26);
           if (ok) {
-            ok = G::kTf32 ? waitBar(&bars->vt_full, j & 1, err, 27)
-                          : waitBar(&bars->v_full[slot], (j >> 1) & 1, err, 27);
+            ok = G::kTf32 ? warpWaitBar(&bars->vt_full, j & 1, err, 27)
+                          : warpWaitBar(&bars->v_full[slot], (j >> 1) & 1, err, 27);
           }
           if (!ok) break;
           tcFenceAfter();
@@ -318,13 +313,14 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
               mmaTS<T>(tmem + kOCol, at, bd, idesc_o, (j > 0 || ks > 0) ? 1u : 0u);
             }
           }
-          tcCommit(&bars->p_free);
-          tcCommit(G::kTf32 ? &bars->vt_empty : &bars->v_empty[slot]);
-          tcCommit(&bars->s_free[slot]);
+          tcCommitElect(&bars->p_free);
+          tcCommitElect(G::kTf32 ? &bars->vt_empty : &bars->v_empty[slot]);
+          tcCommitElect(&bars->s_free[slot]);
         }
       }
-      tcCommit(&bars->o_done);
-      drainBar(&bars->o_done, 0);
+      tcCommitElect(&bars->o_done);
+      if (lane == 0) drainBar(&bars->o_done, 0);
+      __syncwarp();
     }
   } else if (warp < 6) {
     // ---------------- softmax + output (warps 2..5) ----------------

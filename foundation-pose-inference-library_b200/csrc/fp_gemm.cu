@@ -90,21 +90,6 @@ struct Elem {
 };
 
 template <typename T>
-__device__ __forceinline__ void mmaT(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                     uint32_t accumulate) {
-  if constexpr (Elem<T>::kTf32) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-  } else {
-    tcMma(d_tmem, a_desc, b_desc, idesc, accumulate);
-  }
-}
-
-template <typename T>
 __device__ __forceinline__ void mmaTElect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
   if constexpr (Elem<T>::kTf32) {
