@@ -2,7 +2,9 @@
 // self-attention in fp_attention.cu). Planar activations: 16-byte records of
 // 8 (fp16/bf16, "KP8") or 4 (fp32, "KP4") channels.
 //
-//  * layerNormKernel   per-row LayerNorm over 512 channels (planar -> planar)
+//  * layerNorm16Kernel per-row LayerNorm over 512 channels (planar -> planar),
+//                      in registers for fp16/bf16; layerNormKernel (shared-memory
+//                      tile) for fp32
 //  * tokenMeanKernel   mean over the tokens of each sequence (planar -> fp32)
 //  * linearF32Kernel / smallAttentionKernel  fp32 tail of ScoreNet (attention
 //                      across hypotheses) and the 512->3 / 512->1 heads
@@ -100,6 +102,99 @@ __global__ void __launch_bounds__(256) layerNormKernel(LnArgs a) {
       *reinterpret_cast<uint4*>(a.out + static_cast<long long>(plane) * a.out_plane_stride +
                                 (r0 + row) * 16) = *reinterpret_cast<const uint4*>(&tile[row][plane * kPR]);
     }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float2 toF2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 toF2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <>
+__device__ __forceinline__ float2 toF2<__nv_bfloat16>(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t fromF2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t fromF2<__half>(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t fromF2<__nv_bfloat16>(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// LayerNorm over 512 channels of 16-bit planar activations, in registers: a
+// warp normalises 4 rows; lane l holds channel planes g, g+8, ..., g+56
+// (g = l / 4) of row l % 4, so every warp-wide load or store moves 8 planes x
+// 4 consecutive rows (64 contiguous bytes per plane), and all 8 loads of a
+// lane are in flight together. Row statistics: per-lane partial sums, then a
+// butterfly over the 8 lanes of the row.
+template <typename T>
+__global__ void __launch_bounds__(256, 2) layerNorm16Kernel(LnArgs a) {
+  __shared__ float gamma[512], beta[512];
+  for (int i = threadIdx.x; i < 512; i += 256) {
+    gamma[i] = a.gamma[i];
+    beta[i] = a.beta[i];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const long long row = (static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * 4 + (lane & 3);
+  const bool valid = row < a.rows;
+  uint4 rec[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    rec[k] = valid ? *reinterpret_cast<const uint4*>(a.in + static_cast<long long>(g + 8 * k) * a.in_plane_stride +
+                                                     row * 16)
+                   : make_uint4(0, 0, 0, 0);
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = toF2<T>(w[j]);
+      s += f.x + f.y;
+    }
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  const float mean = s * (1.0f / 512.0f);
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = toF2<T>(w[j]);
+      const float d0 = f.x - mean;
+      const float d1 = f.y - mean;
+      q += d0 * d0 + d1 * d1;
+    }
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+  const float rstd = rsqrtf(q * (1.0f / 512.0f) + a.eps);
+  if (!valid) return;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int ch = (g + 8 * k) * 8;
+    const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = toF2<T>(w[j]);
+      const int c = ch + 2 * j;
+      o[j] = fromF2<T>((f.x - mean) * rstd * gamma[c] + beta[c], (f.y - mean) * rstd * gamma[c + 1] + beta[c + 1]);
+    }
+    *reinterpret_cast<uint4*>(a.out + static_cast<long long>(g + 8 * k) * a.out_plane_stride + row * 16) =
+        make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -259,13 +354,13 @@ cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
   switch (dtype) {
     case FPK_DTYPE_BF16:
-      layerNormKernel<__nv_bfloat16, 32><<<static_cast<int>((a.rows + 31) / 32), 256, 0, s>>>(a);
+      layerNorm16Kernel<__nv_bfloat16><<<static_cast<int>((a.rows + 31) / 32), 256, 0, s>>>(a);
       break;
     case FPK_DTYPE_F32:
       layerNormKernel<float, 16><<<static_cast<int>((a.rows + 15) / 16), 256, 0, s>>>(a);
       break;
     default:
-      layerNormKernel<__half, 32><<<static_cast<int>((a.rows + 31) / 32), 256, 0, s>>>(a);
+      layerNorm16Kernel<__half><<<static_cast<int>((a.rows + 31) / 32), 256, 0, s>>>(a);
   }
   return cudaGetLastError();
 }
