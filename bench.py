@@ -41,7 +41,7 @@ sys.path.insert(0, str(PKG / "python"))
 N_HYP = 252
 # gemmKernel DRAM traffic per TFLOP of algorithmic GEMM work, from one ncu
 # capture over whole register calls (profiles/gemm_dram_traffic_register.md).
-GEMM_DRAM_BYTES_PER_TFLOP = 11463.6e6 / 11.60
+GEMM_DRAM_BYTES_PER_TFLOP = 28596.3e6 / 28.99
 N_ITERS = 5
 W, H = 640, 480
 FP16 = 2
