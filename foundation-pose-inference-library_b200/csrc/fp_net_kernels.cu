@@ -7,7 +7,8 @@
 //                      tile) for fp32
 //  * tokenMeanKernel   mean over the tokens of each sequence (planar -> fp32)
 //  * linearF32Kernel / smallAttentionKernel  fp32 tail of ScoreNet (attention
-//                      across hypotheses) and the 512->3 / 512->1 heads
+//                      across hypotheses); linearFewKernel for the 512->3 /
+//                      512->1 heads
 //  * nchwToStemKernel  NCHW fp32 network inputs (the IInferenceRunner seam) to
 //                      the stem's space-to-depth planar layout
 //  * convertKernel     fp32 -> fp16/bf16 weight copies
@@ -211,10 +212,25 @@ __global__ void __launch_bounds__(256) tokenMeanKernel(const unsigned char* __re
   const int sub = threadIdx.x % kSubs;
   const long long base = static_cast<long long>(blockIdx.x) * seq_len;
   float acc[kPR] = {};
-  for (int r = sub; r < seq_len; r += kSubs) {
+  const unsigned char* src = in + static_cast<long long>(plane) * plane_stride + base * 16;
+  // Four rows' records are requested before any is added (the sum keeps the
+  // row order r, r + kSubs, ...), so each thread has four loads in flight.
+  int r = sub;
+  for (; r + 3 * kSubs < seq_len; r += 4 * kSubs) {
+    alignas(16) T rec[4][kPR];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      *reinterpret_cast<uint4*>(rec[u]) = *reinterpret_cast<const uint4*>(src + static_cast<long long>(r + u * kSubs) * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+      for (int i = 0; i < kPR; ++i) acc[i] += toF<T>(rec[u][i]);
+    }
+  }
+  for (; r < seq_len; r += kSubs) {
     alignas(16) T rec[kPR];
-    *reinterpret_cast<uint4*>(rec) = *reinterpret_cast<const uint4*>(
-        in + static_cast<long long>(plane) * plane_stride + (base + r) * 16);
+    *reinterpret_cast<uint4*>(rec) = *reinterpret_cast<const uint4*>(src + static_cast<long long>(r) * 16);
 #pragma unroll
     for (int i = 0; i < kPR; ++i) acc[i] += toF<T>(rec[i]);
   }
@@ -226,6 +242,38 @@ __global__ void __launch_bounds__(256) tokenMeanKernel(const unsigned char* __re
 #pragma unroll
     for (int q = 1; q < kSubs; ++q) t += part[q][c];
     out[blockIdx.x * 512 + c] = t / seq_len;
+  }
+}
+
+// y[m][n] = sum_k x[m][k] * w[n][k] + b[n] (+ relu) for n <= 8 outputs (the
+// 512 -> 3 pose heads and the 512 -> 1 score head): one warp per row, lane j
+// takes k = j, j + 32, ... (coalesced row reads), then a butterfly per output.
+__global__ void __launch_bounds__(256) linearFewKernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                       const float* __restrict__ b, float* __restrict__ y, int m,
+                                                       int n, int k, int relu) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= m) return;
+  float acc[8] = {};
+  const float* xr = x + static_cast<long long>(row) * k;
+  for (int kk = lane; kk < k; kk += 32) {
+    const float xv = xr[kk];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < n) acc[j] = fmaf(xv, __ldg(w + static_cast<long long>(j) * k + kk), acc[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+  }
+  if (lane < n) {
+    float v = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v = lane == j ? acc[j] : v;
+    v += b != nullptr ? b[lane] : 0.0f;
+    y[static_cast<long long>(row) * n + lane] = relu ? fmaxf(v, 0.0f) : v;
   }
 }
 
@@ -384,6 +432,10 @@ cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int
 cudaError_t launchLinearF32(const float* x, const float* w, const float* b, float* y, int m, int n,
                             int k, bool relu, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
+  if (n <= 8) {
+    linearFewKernel<<<(m + 7) / 8, 256, 0, s>>>(x, w, b, y, m, n, k, relu ? 1 : 0);
+    return cudaGetLastError();
+  }
   const dim3 grid((n + 31) / 32, (m + 31) / 32);
   linearF32Kernel<<<grid, 256, 0, s>>>(x, w, b, y, m, n, k, relu ? 1 : 0);
   return cudaGetLastError();
