@@ -5,10 +5,13 @@
 //
 // One CTA per (query tile, layer * head, sequence). A query tile has up to 128
 // rows (TMEM lanes); keys stream in blocks of 64. Warp roles:
-//   warp 0     producer: bulk copies of the Q tile and of K / V key blocks from
-//              the KP8 planar activations ([plane of 8 channels][row][16 B])
-//              straight into the no-swizzle core-matrix layout
-//              [plane][row][16 B] the tensor core reads.
+//   warp 0     producer: one 2-D TMA tile load per Q tile and per K / V key
+//              block from the KP8 planar activations ([plane of 8 channels]
+//              [row][16 B]) straight into the no-swizzle core-matrix layout
+//              [plane][row][16 B] the tensor core reads (per-plane bulk copies,
+//              16 per block, could not be issued as fast as blocks were
+//              consumed); key blocks are requested one block ahead of value
+//              blocks, three in flight.
 //   warp 1     MMA issuer (one lane) + TMEM owner:
 //                S_b = Q K_b^T   (M=128, N=64, K=128; A, B K-major)   -> TMEM
 //                O  += P_b V_b   (M=128, N=128, K=64; A = P from TMEM,
@@ -27,6 +30,7 @@
 // per CTA, so two CTAs share an SM and overlap each other's loads, softmax and
 // MMAs; fp32 activations run kind::tf32 (TF32 math) with 192 KB, one CTA. All mbarrier waits are
 // bounded (fp_tc.cuh) and report through AttnArgs::error_flag.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -67,11 +71,14 @@ struct Geo {
   // planes are padded by 16 bytes (conflict-free column reads). P is kept in
   // shared memory too, as a K-major [4-key plane][row][16 B] tile.
   static constexpr int kThreads = kTf32 ? 256 : 192;
+  // Key blocks in flight: three for 16-bit (a block arrives from DRAM about two
+  // block-times after it is requested), two for fp32 (no shared memory left).
+  static constexpr int kKSlots = kTf32 ? 2 : 3;
   static constexpr uint32_t kVRawPlane = kKeys * 16 + (kTf32 ? 16 : 0);
   static constexpr uint32_t kVBytes = kTf32 ? kPlanes * kVRawPlane : 2 * kKVBytes;
   static constexpr uint32_t kVTBytes = kTf32 ? kKVBytes : 0;
   static constexpr uint32_t kPBytes = kTf32 ? (kKeys / kPerRecord) * kRows * 16 : 0;
-  static constexpr size_t kSmem = 128 + kQBytes + 2 * kKVBytes + kVBytes + kVTBytes + kPBytes + 256;
+  static constexpr size_t kSmem = 128 + kQBytes + kKSlots * kKVBytes + kVBytes + kVTBytes + kPBytes + 256;
   static constexpr int kMinBlocks = kTf32 ? 1 : 2;
   static constexpr uint32_t fmt() { return kTf32 ? 2u : (std::is_same<T, __nv_bfloat16>::value ? 1u : 0u); }
 };
@@ -81,7 +88,7 @@ constexpr float kRescaleLog2 = 8.0f;
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
+  uint64_t k_full[3], k_empty[3];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2];
   uint64_t p_full, p_free;  // P_b ready / PV_b complete
@@ -138,7 +145,9 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentionTcKernel(const net::AttnArgs a) {
+__global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
+    attentionTcKernel(const net::AttnArgs a, const __grid_constant__ CUtensorMap q_map,
+                      const __grid_constant__ CUtensorMap kv_map) {
   using G = Geo<T>;
   constexpr int kPlanes = G::kPlanes;
   constexpr uint32_t kQBytes = G::kQBytes;
@@ -147,8 +156,8 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
   unsigned char* q_s = base;
-  unsigned char* k_s = q_s + kQBytes;           // [2][planes][64 keys][16 B]
-  unsigned char* v_s = k_s + 2 * kKVBytes;      // [2][planes][64 keys][16 B]; fp32: padded staging
+  unsigned char* k_s = q_s + kQBytes;           // [kKSlots][planes][64 keys][16 B]
+  unsigned char* v_s = k_s + G::kKSlots * kKVBytes;  // [2][planes][64 keys][16 B]; fp32: padded staging
   unsigned char* vt_s = v_s + G::kVBytes;       // fp32 only: [16 key planes][128 ch][16 B]
   unsigned char* p_s = vt_s + G::kVTBytes;      // fp32 only: [16 key planes][128 rows][16 B]
   Bars* bars = reinterpret_cast<Bars*>(p_s + G::kPBytes);
@@ -168,9 +177,11 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
 
   if (threadIdx.x == 0) {
     mbarInit(&bars->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < G::kKSlots; ++i) {
       mbarInit(&bars->k_full[i], 1);
       mbarInit(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbarInit(&bars->v_full[i], 1);
       mbarInit(&bars->v_empty[i], G::kTf32 ? 2 : 1);
       mbarInit(&bars->s_full[i], 1);
@@ -202,51 +213,59 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
       // Rows past the sequence (the tile tail, the last key block) read the
       // next sequence or the buffer's zero guard rows: finite values whose
       // scores are masked and whose outputs are not stored.
+      // One tile load per operand block ({rows x 16 B, planes} boxes land as
+      // [plane][row][16 B]); rows past the buffer read as zeros.
       mbarExpectTx(&bars->q_full, kQBytes);
-      for (int p = 0; p < kPlanes; ++p) {
-        bulkCopy(q_s + p * (kRows * 16),
-                 a.qkv + static_cast<long long>(qp + p) * a.qkv_plane_stride + (row_base + q0) * 16,
-                 kRows * 16, &bars->q_full);
-      }
+      tmaLoad2d(q_s, &q_map, static_cast<int>(2 * (row_base + q0)), qp, &bars->q_full);
       bool ok = true;
-      int issued = 0;
-      for (int b = 0; b < n_blocks && ok; ++b) {
-        const int slot = b & 1;
+      int k_issued = 0, v_issued = 0;
+      // Key block b goes to slot b % kKSlots once S_{b - kKSlots} has read it;
+      // key blocks are requested one block ahead of value blocks, so a key
+      // load never waits behind a value slot.
+      auto issueK = [&](int b) -> bool {
+        const int slot = b % G::kKSlots;
+        if (b >= G::kKSlots && !waitBar(&bars->k_empty[slot], ((b / G::kKSlots) - 1) & 1, err, 21)) return false;
         const long long r0 = row_base + static_cast<long long>(b) * kKeys;
-        if (b >= 2) ok = waitBar(&bars->k_empty[slot], ((b >> 1) - 1) & 1, err, 21);
-        if (!ok) break;
         mbarExpectTx(&bars->k_full[slot], kKVBytes);
-        for (int p = 0; p < kPlanes; ++p) {
-          bulkCopy(k_s + slot * kKVBytes + p * (kKeys * 16),
-                   a.qkv + static_cast<long long>(kp + p) * a.qkv_plane_stride + r0 * 16,
-                   kKeys * 16, &bars->k_full[slot]);
-        }
+        tmaLoad2d(k_s + slot * kKVBytes, &kv_map, static_cast<int>(2 * r0), kp, &bars->k_full[slot]);
+        k_issued = b + 1;
+        return true;
+      };
+      ok = issueK(0);
+      for (int b = 0; b < n_blocks && ok; ++b) {
+        if (b + 1 < n_blocks) ok = issueK(b + 1);
+        if (!ok) break;
         // V: double-buffered (16-bit), or one staging buffer (fp32) that the
         // transpose warps release.
+        const int slot = b & 1;
+        const long long r0 = row_base + static_cast<long long>(b) * kKeys;
         const int vslot = G::kTf32 ? 0 : slot;
         if (G::kTf32 ? b >= 1 : b >= 2) {
           ok = waitBar(&bars->v_empty[vslot], G::kTf32 ? ((b - 1) & 1) : (((b >> 1) - 1) & 1), err, 22);
         }
-        if (!ok) {
-          issued = 2 * b + 1;
-          break;
-        }
+        if (!ok) break;
         mbarExpectTx(&bars->v_full[vslot], kKVBytes);
-        for (int p = 0; p < kPlanes; ++p) {
-          bulkCopy(v_s + (G::kTf32 ? p * G::kVRawPlane : slot * kKVBytes + p * (kKeys * 16)),
-                   a.qkv + static_cast<long long>(vp + p) * a.qkv_plane_stride + r0 * 16,
-                   kKeys * 16, &bars->v_full[vslot]);
+        if constexpr (G::kTf32) {
+          // fp32: per-plane copies into the padded staging planes.
+          for (int p = 0; p < kPlanes; ++p) {
+            bulkCopy(v_s + p * G::kVRawPlane, a.qkv + static_cast<long long>(vp + p) * a.qkv_plane_stride + r0 * 16,
+                     kKeys * 16, &bars->v_full[vslot]);
+          }
+        } else {
+          tmaLoad2d(v_s + slot * kKVBytes, &kv_map, static_cast<int>(2 * r0), vp, &bars->v_full[vslot]);
         }
-        issued = 2 * b + 2;
+        v_issued = b + 1;
       }
       // Drain: every copy armed above lands before the CTA may exit.
       drainBar(&bars->q_full, 0);
-      for (int i = issued > 4 ? issued - 4 : 0; i < issued; ++i) {
-        const int b = i >> 1;
-        if ((i & 1) && G::kTf32) {
+      for (int b = k_issued > G::kKSlots ? k_issued - G::kKSlots : 0; b < k_issued; ++b) {
+        drainBar(&bars->k_full[b % G::kKSlots], (b / G::kKSlots) & 1);
+      }
+      for (int b = v_issued > 2 ? v_issued - 2 : 0; b < v_issued; ++b) {
+        if (G::kTf32) {
           drainBar(&bars->v_full[0], b & 1);
         } else {
-          drainBar((i & 1) ? &bars->v_full[b & 1] : &bars->k_full[b & 1], (b >> 1) & 1);
+          drainBar(&bars->v_full[b & 1], (b >> 1) & 1);
         }
       }
     }
@@ -264,8 +283,9 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
       tcFenceAfter();
       for (int b = 0; b <= n_blocks && ok; ++b) {
         if (b < n_blocks) {
-          const int slot = b & 1;
-          ok = warpWaitBar(&bars->k_full[slot], (b >> 1) & 1, err, 24);
+          const int slot = b & 1;               // S buffer
+          const int kslot = b % G::kKSlots;     // key block
+          ok = warpWaitBar(&bars->k_full[kslot], (b / G::kKSlots) & 1, err, 24);
           if (ok && b >= 2) ok = warpWaitBar(&bars->s_free[slot], ((b >> 1) - 1) & 1, err, 25);
           if (!ok) break;
           tcFenceAfter();
@@ -277,12 +297,12 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks) attentio
           for (int ks = 0; ks < kPlanes / 2; ++ks) {
             // 32 bytes of head channels = two planes per K step.
             const uint64_t ad = smemDesc(q_addr + ks * 2 * (kRows * 16), kRows * 16, 128, kLayoutNone);
-            const uint64_t bd = smemDesc(k_addr + slot * kKVBytes + ks * 2 * (kKeys * 16), kKeys * 16,
+            const uint64_t bd = smemDesc(k_addr + kslot * kKVBytes + ks * 2 * (kKeys * 16), kKeys * 16,
                                          128, kLayoutNone);
             mmaSS<T>(d, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
           }
           tcCommitElect(&bars->s_full[slot]);
-          tcCommitElect(&bars->k_empty[slot]);
+          tcCommitElect(&bars->k_empty[kslot]);
         }
         if (b >= 1) {
           const int j = b - 1;
@@ -498,8 +518,17 @@ cudaError_t launch(const net::AttnArgs& a, int layers, int n_seq, cudaStream_t s
     attr_mask |= 1 << dev;
   }
   const int q_tiles = (a.seq_len + kRows - 1) / kRows;
+  // Maps over the whole qkv buffer: every plane of every layer, every row of
+  // every sequence; the kernel indexes blocks by (row, first plane).
+  CUtensorMap q_map, kv_map;
+  const long long rows = static_cast<long long>(n_seq) * a.seq_len;
+  const int planes = layers * a.qkv_layer_planes;
+  if (makePlanarRowsMap(a.qkv, rows, planes, a.qkv_plane_stride, kRows, Geo<T>::kPlanes, &q_map, "fpk_attention") != 0 ||
+      makePlanarRowsMap(a.qkv, rows, planes, a.qkv_plane_stride, kKeys, Geo<T>::kPlanes, &kv_map, "fpk_attention") != 0) {
+    return cudaErrorInvalidValue;
+  }
   prof::countLaunch(prof::kAttention);
-  attentionTcKernel<T><<<dim3(q_tiles, layers * a.heads, n_seq), Geo<T>::kThreads, Geo<T>::kSmem, s>>>(a);
+  attentionTcKernel<T><<<dim3(q_tiles, layers * a.heads, n_seq), Geo<T>::kThreads, Geo<T>::kSmem, s>>>(a, q_map, kv_map);
   return cudaGetLastError();
 }
 

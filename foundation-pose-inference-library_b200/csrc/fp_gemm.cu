@@ -37,6 +37,7 @@
 #include <type_traits>
 #include <unordered_map>
 
+#include "fp_net_kernels.cuh"
 #include "fp_profile.hpp"
 #include "fp_tc.cuh"
 #include "fpk.h"
@@ -763,24 +764,10 @@ int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map
   return 0;
 }
 
-// 3-D map over a planar activation for the CTA-pair kernel: {16-byte record,
-// row, plane}; one box is a window of win_rows rows x `planes` planes, laid
-// out in shared memory exactly like the bulk-copied windows ([plane][row][16 B]).
-// Rows outside [0, rows) read as zeros (the guard rows of the layout are zero).
+// Activation map of the CTA-pair kernel: windows of win_rows rows x `planes`
+// channel planes of the layer input.
 int makeActivationMap(const fpk_gemm_desc_t& d, int total_planes, int win_rows, int planes, CUtensorMap* map) {
-  EncodeTiledFn enc = encodeFn();
-  if (enc == nullptr) return fail("fpk_gemm: cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[3] = {16u, static_cast<cuuint64_t>(d.rows), static_cast<cuuint64_t>(total_planes)};
-  const cuuint64_t strides[2] = {16u, static_cast<cuuint64_t>(d.a_plane_stride)};
-  const cuuint32_t box[3] = {16u, static_cast<cuuint32_t>(win_rows), static_cast<cuuint32_t>(planes)};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(d.a), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    return fail("fpk_gemm: cuTensorMapEncodeTiled (activations) failed (" + std::to_string(r) + ")");
-  }
-  return 0;
+  return makePlanarMap(d.a, d.rows, total_planes, d.a_plane_stride, win_rows, planes, map, "fpk_gemm");
 }
 
 // Splits the shared memory left after the barriers between activation window
@@ -922,6 +909,42 @@ int launchShape(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map
 }
 
 }  // namespace gemm
+
+int makePlanarMap(const void* base, long long rows, int planes, long long plane_stride, int box_rows,
+                  int box_planes, CUtensorMap* map, const char* who) {
+  gemm::EncodeTiledFn enc = gemm::encodeFn();
+  if (enc == nullptr) return fail(std::string(who) + ": cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {16u, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(planes)};
+  const cuuint64_t strides[2] = {16u, static_cast<cuuint64_t>(plane_stride)};
+  const cuuint32_t box[3] = {16u, static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(box_planes)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(std::string(who) + ": cuTensorMapEncodeTiled (planar activations) failed (" + std::to_string(r) + ")");
+  }
+  return 0;
+}
+
+int makePlanarRowsMap(const void* base, long long rows, int planes, long long plane_stride, int box_rows,
+                      int box_planes, CUtensorMap* map, const char* who) {
+  gemm::EncodeTiledFn enc = gemm::encodeFn();
+  if (enc == nullptr) return fail(std::string(who) + ": cuTensorMapEncodeTiled unavailable");
+  if (box_rows <= 0 || box_rows > 128) return fail(std::string(who) + ": planar row box must be 1..128 rows");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(2 * rows), static_cast<cuuint64_t>(planes)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(plane_stride)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(2 * box_rows), static_cast<cuuint32_t>(box_planes)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(std::string(who) + ": cuTensorMapEncodeTiled (planar rows) failed (" + std::to_string(r) + ")");
+  }
+  return 0;
+}
+
 }  // namespace fpb
 
 using namespace fpb;

@@ -238,6 +238,14 @@ __device__ __forceinline__ bool warpWaitBar(uint64_t* bar, uint32_t parity, int*
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+__device__ __forceinline__ void tmaLoad3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4, %5}], [%2];" ::"r"(smemU32(dst)),
+      "l"(map), "r"(smemU32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void tcFenceBefore() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
