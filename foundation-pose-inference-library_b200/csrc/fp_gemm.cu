@@ -1,8 +1,8 @@
 // Persistent tcgen05 implicit-GEMM kernel (sm_100a) for RefineNet / ScoreNet.
 //
 // One CTA per SM walks output tiles of 128 (or, for layers of at most 128
-// output channels, 256) rows x BN channels; convolutions and residual 1x1
-// layers of 256-channel tiles run on CTA pairs instead (gemmPairKernel below).
+// output channels, 256) rows x BN channels; layers with 256-channel tiles run
+// on CTA pairs instead (gemmPairKernel below) when their rows fill the GPU.
 // Warp roles:
 //   warp 0     producer: per 64-channel chunk, one bulk copy per channel plane
 //              brings a window of 128 + span rows of the activation into shared
@@ -112,6 +112,7 @@ struct Plan {
   uint32_t a_win_bytes;  // per slot
   uint32_t b_stage_bytes;
   uint32_t a_slot_bytes;  // CTA-pair kernel: window slot stride (1024-byte aligned)
+  uint32_t a_plane_pitch;  // CTA-pair kernel: bytes between channel planes of a window (128-byte aligned)
 };
 
 template <typename T>
@@ -519,12 +520,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     barriers, which the leader arms with the bytes of both CTAs;
 //   * both CTAs' epilogues wait on their own `acc_full` (signalled by the
 //     leader's commit) and release the buffer on the leader's `acc_empty`.
-// Activation windows are 3-D TMA tiles {16 B record, rows, planes} (zero fill
-// outside the tensor), so the window may not exceed 256 rows.
+// Activation windows are row-run TMA tiles (a plane's rows as one contiguous
+// run of 8-byte elements, zero fill outside the tensor): one box for windows
+// of at most 128 rows, else a 128-row box and a tail box per plane; windows
+// may not exceed 256 rows.
 template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmPairKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_a) {
+                   const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_tail) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -543,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x < pl.stages_per_chunk * 2) {
     constexpr int kStep = 32 / Elem<T>::kBytes;
-    const uint32_t plane_units = static_cast<uint32_t>(pl.win_rows);
+    const uint32_t plane_units = pl.a_plane_pitch >> 4;
     uint32_t packed = 0;
     for (int h = 0; h < 2; ++h) {
       const int k_local = (threadIdx.x * 2 + h) * kStep;
@@ -603,10 +606,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
           ok = warpWaitBar(&sm->a_empty[slot], a_phase ^ 1, err, 21);
           if (!ok) break;
-          if (lane == 0) {
-            if (leader) mbarExpectTx(&sm->a_full[slot], 2u * pl.a_win_bytes);
-            tmaLoad3dPair(a_smem + static_cast<size_t>(slot) * pl.a_slot_bytes, &tmap_a, 0, m0 + row_off,
-                          ch * pl.planes, mapaShared(smemU32(&sm->a_full[slot]), 0));
+          // The window as row-run tiles (each plane's rows are one contiguous
+          // run): one box of every plane when it has at most 128 rows, else a
+          // 128-row box and a tail box per plane, issued by parallel lanes.
+          if (lane == 0 && leader) mbarExpectTx(&sm->a_full[slot], 2u * pl.a_win_bytes);
+          __syncwarp();
+          {
+            unsigned char* win = a_smem + static_cast<size_t>(slot) * pl.a_slot_bytes;
+            const uint32_t bar = mapaShared(smemU32(&sm->a_full[slot]), 0);
+            const int row = m0 + row_off;
+            if (pl.win_rows <= 128) {
+              if (lane == 0) tmaLoad2dPair(win, &tmap_a, 2 * row, ch * pl.planes, bar);
+            } else if (lane < 2 * pl.planes) {
+              const int p = lane < pl.planes ? lane : lane - pl.planes;
+              const bool tail = lane >= pl.planes;
+              tmaLoad2dPair(win + static_cast<size_t>(p) * pl.a_plane_pitch + (tail ? 128 * 16 : 0),
+                            tail ? &tmap_a_tail : &tmap_a, 2 * (row + (tail ? 128 : 0)), ch * pl.planes + p, bar);
+            }
           }
           ++a_iter;
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
@@ -642,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- MMA issuer (leader CTA) ----------------
       const uint32_t idesc = Elem<T>::instrDesc(BN, kPairM);
       const uint64_t a_desc0 =
-          smemDesc(smemU32(a_smem), static_cast<uint32_t>(pl.win_rows) * 16u, 128u, kLayoutNone);
+          smemDesc(smemU32(a_smem), pl.a_plane_pitch, 128u, kLayoutNone);
       const uint64_t b_desc0 = smemDesc(smemU32(b_smem), 16u, 1024u, kLayoutSw128);
       const uint32_t a_slot_units = pl.a_slot_bytes >> 4;
       const uint32_t b_stage_units = pl.b_stage_bytes >> 4;
@@ -764,12 +780,6 @@ int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map
   return 0;
 }
 
-// Activation map of the CTA-pair kernel: windows of win_rows rows x `planes`
-// channel planes of the layer input.
-int makeActivationMap(const fpk_gemm_desc_t& d, int total_planes, int win_rows, int planes, CUtensorMap* map) {
-  return makePlanarMap(d.a, d.rows, total_planes, d.a_plane_stride, win_rows, planes, map, "fpk_gemm");
-}
-
 // Splits the shared memory left after the barriers between activation window
 // slots and weight stages so that the MMAs can run furthest ahead of the
 // loads: the number of weight stages covered by both the window slots in
@@ -832,7 +842,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
 bool g_cta_pairs = true;
 template <typename T, int BN>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
-               size_t smem, cudaStream_t stream) {
+               const CUtensorMap& map_a_tail, size_t smem, cudaStream_t stream) {
   static int attr_mask = 0;
   static std::mutex mu;
   static std::unordered_map<long long, int> clusters_for;  // (device, smem) -> co-resident pairs
@@ -877,7 +887,7 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
   const int tiles = pl.m_tiles * pl.n_tiles;
   cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
   prof::countLaunch(prof::kGemm);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN>, d, pl, map_w, map_a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN>, d, pl, map_w, map_a, map_a_tail);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(std::string("gemmPairKernel launch: ") + cudaGetErrorString(e));
@@ -909,23 +919,6 @@ int launchShape(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map
 }
 
 }  // namespace gemm
-
-int makePlanarMap(const void* base, long long rows, int planes, long long plane_stride, int box_rows,
-                  int box_planes, CUtensorMap* map, const char* who) {
-  gemm::EncodeTiledFn enc = gemm::encodeFn();
-  if (enc == nullptr) return fail(std::string(who) + ": cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[3] = {16u, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(planes)};
-  const cuuint64_t strides[2] = {16u, static_cast<cuuint64_t>(plane_stride)};
-  const cuuint32_t box[3] = {16u, static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(box_planes)};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    return fail(std::string(who) + ": cuTensorMapEncodeTiled (planar activations) failed (" + std::to_string(r) + ")");
-  }
-  return 0;
-}
 
 int makePlanarRowsMap(const void* base, long long rows, int planes, long long plane_stride, int box_rows,
                       int box_planes, CUtensorMap* map, const char* who) {
@@ -1006,11 +999,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   // M=256 x N=128 pair MMA is too short to hide its issue cost.)
   const int kprime = pl.n_chunks * d.taps * pl.cw;
   auto s = static_cast<cudaStream_t>(stream);
-  // 1x1 layers without a residual stay on single-CTA 256 x 256 tiles (eight
-  // MMAs per weight stage); with a residual the pairs' second accumulator
-  // buffer, which overlaps the heavier epilogue with the next tile, wins.
-  const bool pair_shape = d.taps > 1 || d.residual != nullptr;
-  if (g_cta_pairs && bn == 256 && pair_shape && kBlockM + (mx - mn) <= 256) {
+  if (g_cta_pairs && bn == 256 && kBlockM + (mx - mn) <= 256) {
     // For 1x1 layers the weight order does not depend on the chunk width
     // (k' = channel), so wider windows (fewer activation barriers per MMA) are
     // free to choose; the widest that keeps the pipeline as deep is taken.
@@ -1029,8 +1018,12 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
       c.n_chunks = d.cin / cw;
       c.stages_per_chunk = d.taps * cw / stage_elems;
       if (c.stages_per_chunk > kMaxStagesPerChunk) continue;
+      // Bytes moved per window, and its shared-memory footprint: every TMA
+      // destination (a plane, or its tail past row 128) starts on 128 bytes.
       c.a_win_bytes = static_cast<uint32_t>(c.planes * c.win_rows * 16);
-      c.a_slot_bytes = (c.a_win_bytes + 1023u) & ~1023u;
+      c.a_plane_pitch = c.win_rows <= 128 ? static_cast<uint32_t>(c.win_rows * 16)
+                                          : (static_cast<uint32_t>(c.win_rows * 16) + 127u) & ~127u;
+      c.a_slot_bytes = (static_cast<uint32_t>(c.planes) * c.a_plane_pitch + 1023u) & ~1023u;
       if (!chooseSlots(c.a_slot_bytes, c.b_stage_bytes, c.stages_per_chunk, &c.a_slots, &c.b_stages)) continue;
       const int depth = c.a_slots * c.stages_per_chunk < c.b_stages ? c.a_slots * c.stages_per_chunk : c.b_stages;
       if (depth >= best_depth) {
@@ -1044,14 +1037,26 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
                           static_cast<size_t>(pp.a_slots) * pp.a_slot_bytes + sizeof(Smem);
       CUtensorMap map_w, map_a;
       if (makeWeightMap(d, kprime, bn / 2, &map_w) != 0) return 1;
-      if (makeActivationMap(d, d.cin * esize / 16, pp.win_rows, pp.planes, &map_a) != 0) return 1;
+      CUtensorMap map_a_tail;
+      const int total_planes = d.cin * esize / 16;
+      if (pp.win_rows <= 128) {
+        if (makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, pp.win_rows, pp.planes, &map_a,
+                              "fpk_gemm") != 0) {
+          return 1;
+        }
+        map_a_tail = map_a;
+      } else if (makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, 128, 1, &map_a, "fpk_gemm") != 0 ||
+                 makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, pp.win_rows - 128, 1, &map_a_tail,
+                                   "fpk_gemm") != 0) {
+        return 1;
+      }
       switch (d.dtype) {
         case FPK_DTYPE_BF16:
-          return launchPair<__nv_bfloat16, 256>(d, pp, map_w, map_a, smem, s);
+          return launchPair<__nv_bfloat16, 256>(d, pp, map_w, map_a, map_a_tail, smem, s);
         case FPK_DTYPE_F32:
-          return launchPair<float, 256>(d, pp, map_w, map_a, smem, s);
+          return launchPair<float, 256>(d, pp, map_w, map_a, map_a_tail, smem, s);
         default:
-          return launchPair<__half, 256>(d, pp, map_w, map_a, smem, s);
+          return launchPair<__half, 256>(d, pp, map_w, map_a, map_a_tail, smem, s);
       }
     }
   }

@@ -7,19 +7,13 @@
 
 namespace fpb {
 
-// 3-D TMA map over a planar activation ([plane][row][16-byte record]):
-// dims {16 B, rows, planes}, one box = box_rows rows x box_planes planes,
-// landing in shared memory as [plane][row][16 B] (the no-swizzle K-major
-// core-matrix layout the tensor core reads). Rows outside [0, rows) read as
-// zeros. Returns 0, or non-zero with the error recorded (fpk_last_error).
-int makePlanarMap(const void* base, long long rows, int planes, long long plane_stride, int box_rows,
-                  int box_planes, CUtensorMap* map, const char* who);
-
 // 2-D TMA map over a planar activation with the rows of a plane as one
 // contiguous run of 8-byte elements: dims {2 * rows, planes}, one box =
 // box_rows (<= 128) rows x box_planes planes, landing as [plane][row][16 B].
-// Coordinates are (2 * first row, first plane). Long contiguous inner runs
-// move far faster through the TMA unit than 16-byte innermost boxes.
+// Coordinates are (2 * first row, first plane); rows outside [0, rows) read
+// as zeros. Long contiguous inner runs move far faster through the TMA unit
+// than boxes whose innermost dimension is one 16-byte record. Returns 0, or
+// non-zero with the error recorded (fpk_last_error).
 int makePlanarRowsMap(const void* base, long long rows, int planes, long long plane_stride, int box_rows,
                       int box_planes, CUtensorMap* map, const char* who);
 

@@ -127,15 +127,6 @@ __device__ __forceinline__ void tmaLoad2dPair(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
-__device__ __forceinline__ void tmaLoad3dPair(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                              uint32_t bar_cluster) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
-      "{%3, %4, %5}], [%2];" ::"r"(smemU32(dst)),
-      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
 // ---- Warp-wide issue: the whole issuing warp runs the MMA loop (its
 // descriptors and loop state stay warp-uniform) and one lane, chosen by
 // elect.sync, issues each tcgen05 instruction. The warp must be converged.
@@ -236,14 +227,6 @@ __device__ __forceinline__ void tcCommitPairOwnElect(uint64_t* bar) {
 __device__ __forceinline__ bool warpWaitBar(uint64_t* bar, uint32_t parity, int* err, int code) {
   const bool ok = mbarTryWait(bar, parity) || waitBar(bar, parity, err, code);
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-}
-
-__device__ __forceinline__ void tmaLoad3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
-      "{%3, %4, %5}], [%2];" ::"r"(smemU32(dst)),
-      "l"(map), "r"(smemU32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
 }
 
 __device__ __forceinline__ void tcFenceBefore() {

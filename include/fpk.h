@@ -208,10 +208,10 @@ typedef struct fpk_gemm_desc {
 
 FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
 
-/* Convolutions and residual 1x1 layers with 256-channel output tiles (cout a
- * multiple of 256) run as CTA pairs (clusters of two CTAs issuing tcgen05
- * cta_group::2 MMAs on 256-row tiles) when their rows fill every SM;
- * enable = 0 keeps every layer on single-CTA tiles. Process-wide;
+/* Layers with 256-channel output tiles (cout a multiple of 256) run as CTA
+ * pairs (clusters of two CTAs issuing tcgen05 cta_group::2 MMAs on 256-row
+ * tiles) when their rows fill every SM; enable = 0 keeps every layer on
+ * single-CTA tiles. Process-wide;
  * returns the previous setting. No reference counterpart (a tuning switch). */
 FP_API int fpk_gemm_set_cta_pairs(int enable);
 

@@ -66,9 +66,9 @@ def err():
 
 @pytest.fixture(params=[1, 0], ids=["pairs", "single"])
 def cta_pairs(request, fpk):
-    """Runs a test with CTA-pair tiles allowed (the default: convolutions and
-    residual 1x1 layers with 256-channel tiles take them when their rows fill
-    every pair of SMs) and with every layer on single-CTA tiles."""
+    """Runs a test with CTA-pair tiles allowed (the default: layers with
+    256-channel tiles take them when their rows fill every pair of SMs) and
+    with every layer on single-CTA tiles."""
     prev = fpk.lib.fpk_gemm_set_cta_pairs(request.param)
     yield request.param
     fpk.lib.fpk_gemm_set_cta_pairs(prev)
