@@ -40,6 +40,7 @@
 #include <string>
 #include <type_traits>
 
+#include "fp_launch.hpp"
 #include "fp_net_kernels.cuh"
 #include "fp_profile.hpp"
 #include "fp_tc.cuh"
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
   constexpr int kPlanes = G::kPlanes;
   constexpr uint32_t kQBytes = G::kQBytes;
   constexpr uint32_t kKVBytes = G::kKVBytes;
+  pdlTrigger();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -202,6 +204,7 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
   }
   __syncthreads();
   tcFenceAfter();
+  pdlWait();  // the QKV projection is complete from here on
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
@@ -528,8 +531,8 @@ cudaError_t launch(const net::AttnArgs& a, int layers, int n_seq, cudaStream_t s
     return cudaErrorInvalidValue;
   }
   prof::countLaunch(prof::kAttention);
-  attentionTcKernel<T><<<dim3(q_tiles, layers * a.heads, n_seq), Geo<T>::kThreads, Geo<T>::kSmem, s>>>(a, q_map, kv_map);
-  return cudaGetLastError();
+  return launchPdl(attentionTcKernel<T>, dim3(q_tiles, layers * a.heads, n_seq), dim3(Geo<T>::kThreads), Geo<T>::kSmem,
+                   s, a, q_map, kv_map);
 }
 
 }  // namespace attn

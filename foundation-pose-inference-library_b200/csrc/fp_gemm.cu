@@ -37,6 +37,7 @@
 #include <type_traits>
 #include <unordered_map>
 
+#include "fp_launch.hpp"
 #include "fp_net_kernels.cuh"
 #include "fp_profile.hpp"
 #include "fp_tc.cuh"
@@ -304,6 +305,7 @@ __device__ __forceinline__ void epilogueRow(const fpk_gemm_desc_t& d, uint32_t t
 template <typename T, int BN, int MH>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w) {
+  pdlTrigger();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Dynamic shared memory: [B stages][A windows][barriers]; B stages need 1024 B alignment.
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -362,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   tcFenceAfter();
+  pdlWait();  // the previous layer's output (this layer's input) is complete from here on
   const uint32_t tmem = sm->tmem_base;
   const int n_tiles_total = pl.m_tiles * pl.n_tiles;
   const int taps_cw = d.taps * pl.cw;
@@ -528,6 +531,7 @@ template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmPairKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_tail) {
+  pdlTrigger();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -586,6 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // any thread signals the peer or any MMA writes the peer's TMEM.
   clusterSync();
   tcFenceAfter();
+  pdlWait();  // the previous layer's output (this layer's input) is complete from here on
   const uint32_t tmem = sm->tmem_base;
   const int n_tiles_total = pl.m_tiles * pl.n_tiles;
   const int pair_id = static_cast<int>(blockIdx.x >> 1);
@@ -835,7 +840,11 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   const int tiles = pl.m_tiles * pl.n_tiles;
   const int grid = tiles < numSms() ? tiles : numSms();
   prof::countLaunch(prof::kGemm);
-  gemmKernel<T, BN, MH><<<grid, kThreads, smem, stream>>>(d, pl, map);
+  const cudaError_t e = launchPdl(gemmKernel<T, BN, MH>, dim3(grid), dim3(kThreads), smem, stream, d, pl, map);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(std::string("gemmKernel launch: ") + cudaGetErrorString(e));
+  }
   return checkLaunch("gemmKernel");
 }
 
@@ -857,17 +866,19 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
     }
     attr_mask |= 1 << dev;
   }
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see fp_launch.hpp
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // the occupancy query below takes the cluster shape only
   int clusters = 0;
   {
     std::lock_guard<std::mutex> lock(mu);
@@ -886,6 +897,7 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
   }
   const int tiles = pl.m_tiles * pl.n_tiles;
   cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
+  cfg.numAttrs = 2;
   prof::countLaunch(prof::kGemm);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN>, d, pl, map_w, map_a, map_a_tail);
   if (e != cudaSuccess) {

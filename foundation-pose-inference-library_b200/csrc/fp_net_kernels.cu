@@ -18,6 +18,7 @@
 
 #include <cstdint>
 
+#include "fp_launch.hpp"
 #include "fp_net_kernels.cuh"
 #include "fpk.h"
 #include "fp_profile.hpp"
@@ -51,6 +52,8 @@ __device__ __forceinline__ float cvt<float>(float v) { return tc::tf32Round(v); 
 // (fp32) channels.
 template <typename T, int R>
 __global__ void __launch_bounds__(256) layerNormKernel(LnArgs a) {
+  tc::pdlTrigger();
+  tc::pdlWait();
   constexpr int kPR = 16 / static_cast<int>(sizeof(T));
   constexpr int kPlanes = 512 / kPR;
   constexpr int kLd = 512 + kPR;  // padded row, keeps 16-byte records aligned
@@ -137,12 +140,14 @@ __device__ __forceinline__ uint32_t fromF2<__nv_bfloat16>(float lo, float hi) {
 // butterfly over the 8 lanes of the row.
 template <typename T>
 __global__ void __launch_bounds__(256, 2) layerNorm16Kernel(LnArgs a) {
+  tc::pdlTrigger();
   __shared__ float gamma[512], beta[512];
   for (int i = threadIdx.x; i < 512; i += 256) {
     gamma[i] = a.gamma[i];
     beta[i] = a.beta[i];
   }
   __syncthreads();
+  tc::pdlWait();  // weights above; activations from here on
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
   const long long row = (static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * 4 + (lane & 3);
@@ -204,6 +209,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) tokenMeanKernel(const unsigned char* __restrict__ in,
                                                        long long plane_stride, int seq_len,
                                                        float* __restrict__ out) {
+  tc::pdlTrigger();
+  tc::pdlWait();
   constexpr int kPR = 16 / static_cast<int>(sizeof(T));
   constexpr int kPlanes = 512 / kPR;
   constexpr int kSubs = 256 / kPlanes;  // row interleave per plane: 4 (16-bit) or 2 (fp32)
@@ -251,6 +258,8 @@ __global__ void __launch_bounds__(256) tokenMeanKernel(const unsigned char* __re
 __global__ void __launch_bounds__(256) linearFewKernel(const float* __restrict__ x, const float* __restrict__ w,
                                                        const float* __restrict__ b, float* __restrict__ y, int m,
                                                        int n, int k, int relu) {
+  tc::pdlTrigger();
+  tc::pdlWait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= m) return;
@@ -282,6 +291,8 @@ __global__ void __launch_bounds__(256) linearF32Kernel(const float* __restrict__
                                                        const float* __restrict__ w,
                                                        const float* __restrict__ b, float* __restrict__ y,
                                                        int m, int n, int k, int relu) {
+  tc::pdlTrigger();
+  tc::pdlWait();
   __shared__ float xs[32][33];
   __shared__ float ws[32][33];
   const int tx = threadIdx.x & 31;
@@ -317,6 +328,8 @@ __global__ void __launch_bounds__(256) linearF32Kernel(const float* __restrict__
 // qkv [len][3*512], 4 heads of 128; one CTA per (query, head).
 __global__ void __launch_bounds__(128) smallAttentionKernel(const float* __restrict__ qkv, int len,
                                                             float* __restrict__ out) {
+  tc::pdlTrigger();
+  tc::pdlWait();
   extern __shared__ float sc[];
   __shared__ float red[4];
   const int i = blockIdx.x;
@@ -402,15 +415,12 @@ cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
   switch (dtype) {
     case FPK_DTYPE_BF16:
-      layerNorm16Kernel<__nv_bfloat16><<<static_cast<int>((a.rows + 31) / 32), 256, 0, s>>>(a);
-      break;
+      return launchPdl(layerNorm16Kernel<__nv_bfloat16>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
     case FPK_DTYPE_F32:
-      layerNormKernel<float, 16><<<static_cast<int>((a.rows + 15) / 16), 256, 0, s>>>(a);
-      break;
+      return launchPdl(layerNormKernel<float, 16>, dim3(static_cast<unsigned>((a.rows + 15) / 16)), dim3(256), 0, s, a);
     default:
-      layerNorm16Kernel<__half><<<static_cast<int>((a.rows + 31) / 32), 256, 0, s>>>(a);
+      return launchPdl(layerNorm16Kernel<__half>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int seq_len, int n_seq,
@@ -418,33 +428,28 @@ cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int
   prof::countLaunch(prof::kOther);
   switch (dtype) {
     case FPK_DTYPE_BF16:
-      tokenMeanKernel<__nv_bfloat16><<<n_seq, 256, 0, s>>>(in, plane_stride, seq_len, out);
-      break;
+      return launchPdl(tokenMeanKernel<__nv_bfloat16>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
     case FPK_DTYPE_F32:
-      tokenMeanKernel<float><<<n_seq, 256, 0, s>>>(in, plane_stride, seq_len, out);
-      break;
+      return launchPdl(tokenMeanKernel<float>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
     default:
-      tokenMeanKernel<__half><<<n_seq, 256, 0, s>>>(in, plane_stride, seq_len, out);
+      return launchPdl(tokenMeanKernel<__half>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launchLinearF32(const float* x, const float* w, const float* b, float* y, int m, int n,
                             int k, bool relu, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
   if (n <= 8) {
-    linearFewKernel<<<(m + 7) / 8, 256, 0, s>>>(x, w, b, y, m, n, k, relu ? 1 : 0);
-    return cudaGetLastError();
+    return launchPdl(linearFewKernel, dim3((m + 7) / 8), dim3(256), 0, s, x, w, b, y, m, n, k, relu ? 1 : 0);
   }
   const dim3 grid((n + 31) / 32, (m + 31) / 32);
-  linearF32Kernel<<<grid, 256, 0, s>>>(x, w, b, y, m, n, k, relu ? 1 : 0);
-  return cudaGetLastError();
+  return launchPdl(linearF32Kernel, grid, dim3(256), 0, s, x, w, b, y, m, n, k, relu ? 1 : 0);
 }
 
 cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
-  smallAttentionKernel<<<dim3(len, 4), 128, static_cast<size_t>(len) * sizeof(float), s>>>(qkv, len, out);
-  return cudaGetLastError();
+  return launchPdl(smallAttentionKernel, dim3(len, 4), dim3(128), static_cast<size_t>(len) * sizeof(float), s, qkv, len,
+                   out);
 }
 
 cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n, int H, int W,

@@ -16,6 +16,11 @@ namespace tc {
 
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
+// Programmatic dependent launch (see fp_launch.hpp): allow the next kernel in
+// the stream to be scheduled / wait for the previous one to complete.
+__device__ __forceinline__ void pdlTrigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdlWait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smemU32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -19,6 +19,8 @@
 #include <type_traits>
 
 #include "fp_device.cuh"
+#include "fp_launch.hpp"
+#include "fp_tc.cuh"
 #include "fp_profile.hpp"
 #include "fpk.h"
 
@@ -694,6 +696,8 @@ __device__ __forceinline__ void storeS2d(void* net, long long plane_stride, int 
 // Vertex pass: crop box and, per vertex, clip position and pixel position
 // under each hypothesis (once per vertex instead of once per triangle corner).
 __global__ void __launch_bounds__(256) vertexKernel(RenderArgs a) {
+  tc::pdlTrigger();
+  tc::pdlWait();
   __shared__ HypState hs;
   const int hyp = blockIdx.y;
   const int tid = threadIdx.x;
@@ -717,6 +721,7 @@ __global__ void __launch_bounds__(256) vertexKernel(RenderArgs a) {
 // Raster pass: one CTA per (row band, hypothesis), z-buffer of packed
 // (depth, triangle) keys in shared memory; writes the band's triangle ids.
 __global__ void __launch_bounds__(kRenderThreads, 1) rasterKernel(RenderArgs a) {
+  tc::pdlTrigger();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned long long* zbuf = reinterpret_cast<unsigned long long*>(smem_raw);
   const int width = a.p.input_width;
@@ -735,6 +740,7 @@ __global__ void __launch_bounds__(kRenderThreads, 1) rasterKernel(RenderArgs a) 
   if (tid == 0) big_count = 0;
   for (int i = tid; i < band_rows * width; i += kRenderThreads) zbuf[i] = ~0ull;
   __syncthreads();
+  tc::pdlWait();  // the vertex pass is complete from here on
 
   const float inv_w = 1.0f / static_cast<float>(width);
   const float inv_h = 1.0f / static_cast<float>(height);
@@ -822,7 +828,9 @@ __global__ void __launch_bounds__(kShadeThreads) shadeKernel(RenderArgs a) {
   const int height = a.p.input_height;
   const int hyp = blockIdx.y;  // grid: (pixel blocks, hypotheses)
   const int tid = threadIdx.x;
+  tc::pdlTrigger();
   lut255[tid] = static_cast<float>(tid) / 255.0f;
+  tc::pdlWait();  // the raster (triangle ids) is complete from here on
   if (tid < 12) hs.pose[tid] = a.poses[hyp * 16 + tid];
   if (tid == 0) hs.box = hypothesisBox(a, hyp);
   __syncthreads();
@@ -1140,11 +1148,15 @@ int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStr
     prof::countLaunch(prof::kRender);
     prof::countLaunch(prof::kRender);
     prof::Scope scope(prof::kRender, bytes, stream);
-    vertexKernel<<<dim3((a.mesh.n_vertices + 255) / 256, a.n), 256, 0, stream>>>(a);
-    rasterKernel<<<dim3(nb, a.n), kRenderThreads, smem, stream>>>(a);
-    shadeKernel<kOut><<<dim3((a.p.input_width * a.p.input_height + kShadeThreads - 1) / kShadeThreads, a.n),
-                        kShadeThreads, 0, stream>>>(a);
-    rc = checkLaunch("render kernels");
+    cudaError_t e = launchPdl(vertexKernel, dim3((a.mesh.n_vertices + 255) / 256, a.n), dim3(256), 0, stream, a);
+    if (e == cudaSuccess) e = launchPdl(rasterKernel, dim3(nb, a.n), dim3(kRenderThreads), smem, stream, a);
+    if (e == cudaSuccess) {
+      e = launchPdl(shadeKernel<kOut>,
+                    dim3((a.p.input_width * a.p.input_height + kShadeThreads - 1) / kShadeThreads, a.n),
+                    dim3(kShadeThreads), 0, stream, a);
+    }
+    if (e != cudaSuccess) cudaGetLastError();
+    rc = e != cudaSuccess ? fail(std::string("render kernels: ") + cudaGetErrorString(e)) : checkLaunch("render kernels");
   }
   if (workspace == nullptr) cudaFreeAsync(mem, stream);
   return rc;
