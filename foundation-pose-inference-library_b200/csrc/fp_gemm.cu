@@ -509,25 +509,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// CTA-pair variant (clusters of two CTAs, tcgen05 cta_group::2) for layers
-// with 256-channel tiles. A pair owns tiles of 256 rows x BN
-// channels: CTA r (r = 0 leader, 1 peer) stages the activation window of rows
-// m0 + 128 r and weight rows n0 + r BN/2 .. + BN/2 in its own shared memory,
-// and the leader's MMA lane issues M=256 x N=BN MMAs that read A from each CTA
-// and B half from each; accumulator rows 0-127 land in the leader's TMEM,
-// 128-255 in the peer's. Per SM this halves the weight bytes staged and read
-// per MMA, which is what limits the single-CTA 128 x 256 tile (shared-memory
-// bandwidth), and leaves room for two accumulator buffers at BN = 256.
+// CTA-pair variant (clusters of two CTAs, tcgen05 cta_group::2). A pair owns
+// tiles of 2 * MH * 128 rows x BN channels: CTA r (r = 0 leader, 1 peer)
+// stages the activation window of its MH * 128 rows and weight rows
+// n0 + r BN/2 .. + BN/2 in its own shared memory, and the leader's MMA lane
+// issues, per K step and row half h < MH, an M=256 x N=BN MMA that reads
+// 128 rows of A from each CTA and B half from each; accumulator rows of CTA r
+// land in its own TMEM (MH blocks of BN columns per buffer). Per SM this
+// halves the weight bytes staged and read per MMA, which is what limits the
+// single-CTA tiles (shared-memory bandwidth), and leaves room for two
+// accumulator buffers. BN = 256 with MH = 1, or BN = 128 with MH = 2.
 //   * both producers wait on their own `empty` barriers (the leader's commits
 //     signal both CTAs) and count their tile loads on the leader's `full`
 //     barriers, which the leader arms with the bytes of both CTAs;
 //   * both CTAs' epilogues wait on their own `acc_full` (signalled by the
 //     leader's commit) and release the buffer on the leader's `acc_empty`.
 // Activation windows are row-run TMA tiles (a plane's rows as one contiguous
-// run of 8-byte elements, zero fill outside the tensor): one box for windows
-// of at most 128 rows, else a 128-row box and a tail box per plane; windows
-// may not exceed 256 rows.
-template <typename T, int BN>
+// run of 8-byte elements, zero fill outside the tensor): one box of all
+// planes for windows of at most 128 rows, else per plane boxes of 128 rows
+// and a tail box, issued by parallel lanes.
+template <typename T, int BN, int MH>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmPairKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_tail) {
@@ -544,8 +545,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = clusterCtaRank();
   const bool leader = rank == 0;
   int* err = d.error_flag;
-  constexpr uint32_t kTmemCols = 2 * BN;  // two accumulator buffers of 128 lanes x BN
-  constexpr int kPairM = 2 * kBlockM;
+  constexpr uint32_t kTmemCols = 2 * MH * BN;  // two accumulator buffers of MH blocks of 128 lanes x BN
+  constexpr int kCtaM = MH * kBlockM;          // output rows per CTA per tile
+  constexpr int kPairM = 2 * kCtaM;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 
   if (threadIdx.x < pl.stages_per_chunk * 2) {
@@ -603,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int slot = 0, bs = 0;
       uint32_t a_phase = 0, b_phase = 0, a_iter = 0, b_iter = 0;
       bool ok = true;
-      const int row_off = static_cast<int>(rank) * kBlockM + pl.min_off;
+      const int row_off = static_cast<int>(rank) * kCtaM + pl.min_off;
       const int n_off = static_cast<int>(rank) * (BN / 2);
       for (int tile = pair_id; tile < n_tiles_total && ok; tile += n_pairs) {
         const int m0 = (tile / pl.n_tiles) * kPairM;
@@ -612,8 +614,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = warpWaitBar(&sm->a_empty[slot], a_phase ^ 1, err, 21);
           if (!ok) break;
           // The window as row-run tiles (each plane's rows are one contiguous
-          // run): one box of every plane when it has at most 128 rows, else a
-          // 128-row box and a tail box per plane, issued by parallel lanes.
+          // run): one box of every plane when it has at most 128 rows, else
+          // per plane ceil(rows / 128) boxes (the last one the tail map's
+          // size), lane c * planes + p issuing box c of plane p.
           if (lane == 0 && leader) mbarExpectTx(&sm->a_full[slot], 2u * pl.a_win_bytes);
           __syncwarp();
           {
@@ -622,11 +625,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = m0 + row_off;
             if (pl.win_rows <= 128) {
               if (lane == 0) tmaLoad2dPair(win, &tmap_a, 2 * row, ch * pl.planes, bar);
-            } else if (lane < 2 * pl.planes) {
-              const int p = lane < pl.planes ? lane : lane - pl.planes;
-              const bool tail = lane >= pl.planes;
-              tmaLoad2dPair(win + static_cast<size_t>(p) * pl.a_plane_pitch + (tail ? 128 * 16 : 0),
-                            tail ? &tmap_a_tail : &tmap_a, 2 * (row + (tail ? 128 : 0)), ch * pl.planes + p, bar);
+            } else {
+              const int n_box = (pl.win_rows + 127) / 128;
+              if (lane < n_box * pl.planes) {
+                const int c = lane / pl.planes;
+                const int p = lane - c * pl.planes;
+                const bool tail = c == n_box - 1 && (pl.win_rows & 127) != 0;
+                tmaLoad2dPair(win + static_cast<size_t>(p) * pl.a_plane_pitch + static_cast<size_t>(c) * 128 * 16,
+                              tail ? &tmap_a_tail : &tmap_a, 2 * (row + 128 * c), ch * pl.planes + p, bar);
+              }
             }
           }
           ++a_iter;
@@ -661,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (leader) {
       // ---------------- MMA issuer (leader CTA) ----------------
-      const uint32_t idesc = Elem<T>::instrDesc(BN, kPairM);
+      const uint32_t idesc = Elem<T>::instrDesc(BN, 2 * kBlockM);  // every pair MMA is M = 256
       const uint64_t a_desc0 =
           smemDesc(smemU32(a_smem), pl.a_plane_pitch, 128u, kLayoutNone);
       const uint64_t b_desc0 = smemDesc(smemU32(b_smem), 16u, 1024u, kLayoutSw128);
@@ -675,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = warpWaitBar(&sm->acc_empty[buf], ((t_iter >> 1) & 1) ^ 1, err, 23);
         if (!ok) break;
         tcFenceAfter();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * MH * BN);
         uint32_t accumulate = 0;
         for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
           ok = warpWaitBar(&sm->a_full[slot], a_phase, err, 24);
@@ -688,16 +695,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tcFenceAfter();
             const uint64_t b_base = b_desc0 + static_cast<uint64_t>(bs) * b_stage_units;
-            if constexpr (Elem<T>::kTf32) {
-              tcMmaPairTf32Elect(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-              tcMmaPairTf32Elect(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
-              tcMmaPairTf32Elect(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-              tcMmaPairTf32Elect(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
-            } else {
-              tcMmaPairF16Elect(d_tmem, a_base + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
-              tcMmaPairF16Elect(d_tmem, a_base + (offs.x >> 16), b_base + 2, idesc, 1u);
-              tcMmaPairF16Elect(d_tmem, a_base + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
-              tcMmaPairF16Elect(d_tmem, a_base + (offs.y >> 16), b_base + 6, idesc, 1u);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {
+              // Row half h reads the window 128 rows (128 units of 16 B) further on.
+              const uint64_t ah = a_base + static_cast<uint64_t>(h * 128);
+              const uint32_t dh = d_tmem + static_cast<uint32_t>(h * BN);
+              if constexpr (Elem<T>::kTf32) {
+                tcMmaPairTf32Elect(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+                tcMmaPairTf32Elect(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
+                tcMmaPairTf32Elect(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+                tcMmaPairTf32Elect(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
+              } else {
+                tcMmaPairF16Elect(dh, ah + (offs.x & 0xFFFFu), b_base, idesc, accumulate);
+                tcMmaPairF16Elect(dh, ah + (offs.x >> 16), b_base + 2, idesc, 1u);
+                tcMmaPairF16Elect(dh, ah + (offs.y & 0xFFFFu), b_base + 4, idesc, 1u);
+                tcMmaPairF16Elect(dh, ah + (offs.y >> 16), b_base + 6, idesc, 1u);
+              }
             }
             accumulate = 1u;
             tcCommitPairBothElect(&sm->b_empty[bs]);
@@ -714,9 +727,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;  // which half of the BN columns this warp converts
-    constexpr int kSpan = BN / 2;
-    const int row_in_tile = static_cast<int>(rank) * kBlockM + quarter * 32 + lane;
+    const int pair = (warp - 2) >> 2;  // MH=1: half of the BN columns; MH=2: row half
+    constexpr int kSpan = MH == 1 ? BN / 2 : BN;  // columns converted by one warp
+    const int m_half = MH == 1 ? 0 : pair;
+    const int row_in_tile = static_cast<int>(rank) * kCtaM + m_half * kBlockM + quarter * 32 + lane;
     uint32_t t_iter = 0;
     for (int tile = pair_id; tile < n_tiles_total; tile += n_pairs, ++t_iter) {
       const int m0 = (tile / pl.n_tiles) * kPairM;
@@ -724,8 +738,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = static_cast<int>(t_iter & 1);
       if (!waitBar(&sm->acc_full[buf], (t_iter >> 1) & 1, err, 27)) break;
       tcFenceAfter();
-      const uint32_t t_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
-      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, half * kSpan);
+      const uint32_t t_base =
+          tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>((buf * MH + m_half) * BN);
+      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, MH == 1 ? pair * kSpan : 0);
       tcFenceBefore();
       __syncwarp();
       if (lane == 0) mbarArriveCluster(mapaShared(smemU32(&sm->acc_empty[buf]), 0));
@@ -849,7 +864,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
 }
 
 bool g_cta_pairs = true;
-template <typename T, int BN>
+template <typename T, int BN, int MH>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
                const CUtensorMap& map_a_tail, size_t smem, cudaStream_t stream) {
   static int attr_mask = 0;
@@ -858,7 +873,7 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 31 && !(attr_mask & (1 << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(gemmPairKernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const cudaError_t e = cudaFuncSetAttribute(gemmPairKernel<T, BN, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) {
       cudaGetLastError();
@@ -886,7 +901,7 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
     auto it = clusters_for.find(key);
     if (it == clusters_for.end()) {
       cfg.gridDim = dim3(2 * (numSms() / 2));
-      if (cudaOccupancyMaxActiveClusters(&clusters, gemmPairKernel<T, BN>, &cfg) != cudaSuccess || clusters < 1) {
+      if (cudaOccupancyMaxActiveClusters(&clusters, gemmPairKernel<T, BN, MH>, &cfg) != cudaSuccess || clusters < 1) {
         cudaGetLastError();
         clusters = numSms() / 2;
       }
@@ -899,7 +914,7 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
   cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
   cfg.numAttrs = 2;
   prof::countLaunch(prof::kGemm);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN>, d, pl, map_w, map_a, map_a_tail);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN, MH>, d, pl, map_w, map_a, map_a_tail);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(std::string("gemmPairKernel launch: ") + cudaGetErrorString(e));
@@ -1005,20 +1020,24 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     pl.n_tiles = d.cout / bn;
     return chooseSlots(pl.a_win_bytes, pl.b_stage_bytes, pl.stages_per_chunk, &pl.a_slots, &pl.b_stages);
   };
-  // CTA pairs (256-row tiles over two SMs) for 256-channel tiles whose
-  // activation window fits one TMA box, when there are pair tiles for every
-  // pair of SMs. (At 128 channels the single-CTA 256-row tiles are faster: an
-  // M=256 x N=128 pair MMA is too short to hide its issue cost.)
+  // CTA pairs over two SMs when there are pair tiles for every pair of SMs:
+  // 256-channel tiles with 256-row pair tiles (one row block per CTA), and
+  // 128-channel layers with 512-row pair tiles (two row blocks per CTA, two
+  // M=256 MMAs per K step, like the single-CTA 256-row tiles, with half the
+  // weight tile staged per SM). Windows of up to 3 x 128 rows.
   const int kprime = pl.n_chunks * d.taps * pl.cw;
   auto s = static_cast<cudaStream_t>(stream);
-  if (g_cta_pairs && bn == 256 && kBlockM + (mx - mn) <= 256) {
+  const int pair_mh = bn == 256 ? 1 : 2;
+  const int pair_planes = pl.cw * esize / 16;
+  if (g_cta_pairs && (bn == 256 || (bn == 128 && d.cout == 128)) &&
+      pair_mh * kBlockM + (mx - mn) <= 3 * 128 && 3 * pair_planes <= 32) {
     // For 1x1 layers the weight order does not depend on the chunk width
     // (k' = channel), so wider windows (fewer activation barriers per MMA) are
     // free to choose; the widest that keeps the pipeline as deep is taken.
     Plan pp = pl;
-    pp.win_rows = kBlockM + (mx - mn);
+    pp.win_rows = pair_mh * kBlockM + (mx - mn);
     pp.b_stage_bytes = static_cast<uint32_t>(bn / 2) * 128u;
-    pp.m_tiles = (d.rows + 2 * kBlockM - 1) / (2 * kBlockM);
+    pp.m_tiles = (d.rows + 2 * pair_mh * kBlockM - 1) / (2 * pair_mh * kBlockM);
     pp.n_tiles = d.cout / bn;
     bool planned = false;
     int best_depth = 0;
@@ -1031,7 +1050,8 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
       c.stages_per_chunk = d.taps * cw / stage_elems;
       if (c.stages_per_chunk > kMaxStagesPerChunk) continue;
       // Bytes moved per window, and its shared-memory footprint: every TMA
-      // destination (a plane, or its tail past row 128) starts on 128 bytes.
+      // destination (a plane, or its boxes past row 128) starts on 128 bytes.
+      if (c.win_rows > 128 && ((c.win_rows + 127) / 128) * c.planes > 32) continue;  // one lane per box
       c.a_win_bytes = static_cast<uint32_t>(c.planes * c.win_rows * 16);
       c.a_plane_pitch = c.win_rows <= 128 ? static_cast<uint32_t>(c.win_rows * 16)
                                           : (static_cast<uint32_t>(c.win_rows * 16) + 127u) & ~127u;
@@ -1057,18 +1077,23 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
           return 1;
         }
         map_a_tail = map_a;
-      } else if (makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, 128, 1, &map_a, "fpk_gemm") != 0 ||
-                 makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, pp.win_rows - 128, 1, &map_a_tail,
-                                   "fpk_gemm") != 0) {
-        return 1;
+      } else {
+        const int tail_rows = (pp.win_rows & 127) != 0 ? (pp.win_rows & 127) : 128;
+        if (makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, 128, 1, &map_a, "fpk_gemm") != 0 ||
+            makePlanarRowsMap(d.a, d.rows, total_planes, d.a_plane_stride, tail_rows, 1, &map_a_tail, "fpk_gemm") != 0) {
+          return 1;
+        }
       }
       switch (d.dtype) {
         case FPK_DTYPE_BF16:
-          return launchPair<__nv_bfloat16, 256>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256 ? launchPair<__nv_bfloat16, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                           : launchPair<__nv_bfloat16, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
         case FPK_DTYPE_F32:
-          return launchPair<float, 256>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256 ? launchPair<float, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                           : launchPair<float, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
         default:
-          return launchPair<__half, 256>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256 ? launchPair<__half, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                           : launchPair<__half, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
       }
     }
   }

@@ -67,8 +67,8 @@ def err():
 @pytest.fixture(params=[1, 0], ids=["pairs", "single"])
 def cta_pairs(request, fpk):
     """Runs a test with CTA-pair tiles allowed (the default: layers with
-    256-channel tiles take them when their rows fill every pair of SMs) and
-    with every layer on single-CTA tiles."""
+    256-channel tiles, and 128-channel layers, take them when their rows fill
+    every pair of SMs) and with every layer on single-CTA tiles."""
     prev = fpk.lib.fpk_gemm_set_cta_pairs(request.param)
     yield request.param
     fpk.lib.fpk_gemm_set_cta_pairs(prev)
@@ -274,11 +274,13 @@ def test_tokens_epilogue(fpk, err, cta_pairs, n):
 
 
 @pytest.mark.parametrize("dtype,cout,cin", [(FPK_DTYPE_F16, 256, 256), (FPK_DTYPE_BF16, 512, 256),
-                                            (FPK_DTYPE_F32, 256, 256)])
+                                            (FPK_DTYPE_F32, 256, 256), (FPK_DTYPE_F16, 128, 128),
+                                            (FPK_DTYPE_BF16, 128, 256), (FPK_DTYPE_F32, 128, 128)])
 def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout, cin):
     """A 3x3 conv with enough rows for pair tiles gives the same bits on CTA
-    pairs (M=256 cta_group::2 MMAs) as on single-CTA tiles: both accumulate
-    every output over the same K sequence in fp32."""
+    pairs (M=256 cta_group::2 MMAs; 512-row pair tiles at 128 channels) as on
+    single-CTA tiles: both accumulate every output over the same K sequence in
+    fp32."""
     g = torch.Generator().manual_seed(11)
     dt = DT[dtype]
     n, H = 30, 40
