@@ -1022,15 +1022,17 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   };
   // CTA pairs over two SMs when there are pair tiles for every pair of SMs:
   // 256-channel tiles with 256-row pair tiles (one row block per CTA), and
-  // 128-channel layers with 512-row pair tiles (two row blocks per CTA, two
-  // M=256 MMAs per K step, like the single-CTA 256-row tiles, with half the
-  // weight tile staged per SM). Windows of up to 3 x 128 rows.
+  // 64- or 128-channel layers with 512-row pair tiles (two row blocks per CTA,
+  // two M=256 MMAs per K step, like the single-CTA 256-row tiles, with half
+  // the weight tile staged per SM and one issuing thread for both SMs).
+  // Windows of up to 4 x 128 rows, one lane per row-run box.
   const int kprime = pl.n_chunks * d.taps * pl.cw;
   auto s = static_cast<cudaStream_t>(stream);
   const int pair_mh = bn == 256 ? 1 : 2;
   const int pair_planes = pl.cw * esize / 16;
-  if (g_cta_pairs && (bn == 256 || (bn == 128 && d.cout == 128)) &&
-      pair_mh * kBlockM + (mx - mn) <= 3 * 128 && 3 * pair_planes <= 32) {
+  const int pair_boxes = (pair_mh * kBlockM + (mx - mn) + 127) / 128;  // row-run boxes per window plane
+  if (g_cta_pairs && (bn == 256 || (bn <= 128 && d.cout == bn)) && pair_boxes <= 4 &&
+      (pair_boxes == 1 || pair_boxes * pair_planes <= 32)) {
     // For 1x1 layers the weight order does not depend on the chunk width
     // (k' = channel), so wider windows (fewer activation barriers per MMA) are
     // free to choose; the widest that keeps the pipeline as deep is taken.
@@ -1086,14 +1088,17 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
       }
       switch (d.dtype) {
         case FPK_DTYPE_BF16:
-          return bn == 256 ? launchPair<__nv_bfloat16, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                           : launchPair<__nv_bfloat16, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256   ? launchPair<__nv_bfloat16, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                 : bn == 128 ? launchPair<__nv_bfloat16, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                             : launchPair<__nv_bfloat16, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
         case FPK_DTYPE_F32:
-          return bn == 256 ? launchPair<float, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                           : launchPair<float, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256   ? launchPair<float, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                 : bn == 128 ? launchPair<float, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                             : launchPair<float, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
         default:
-          return bn == 256 ? launchPair<__half, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                           : launchPair<__half, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256   ? launchPair<__half, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                 : bn == 128 ? launchPair<__half, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
+                             : launchPair<__half, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
       }
     }
   }

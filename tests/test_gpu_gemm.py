@@ -67,8 +67,8 @@ def err():
 @pytest.fixture(params=[1, 0], ids=["pairs", "single"])
 def cta_pairs(request, fpk):
     """Runs a test with CTA-pair tiles allowed (the default: layers with
-    256-channel tiles, and 128-channel layers, take them when their rows fill
-    every pair of SMs) and with every layer on single-CTA tiles."""
+    256-channel tiles, and 64- or 128-channel layers, take them when their rows
+    fill every pair of SMs) and with every layer on single-CTA tiles."""
     prev = fpk.lib.fpk_gemm_set_cta_pairs(request.param)
     yield request.param
     fpk.lib.fpk_gemm_set_cta_pairs(prev)
@@ -214,7 +214,7 @@ def test_s2d_stride2_conv(fpk, err, dtype):
 
 
 @pytest.mark.parametrize("dtype,n", [(FPK_DTYPE_BF16, 2), (FPK_DTYPE_F16, 8), (FPK_DTYPE_F32, 8)])
-def test_stem_7x7_stride2(fpk, err, dtype, n):
+def test_stem_7x7_stride2(fpk, err, cta_pairs, dtype, n):
     """7x7 stride-2 pad-3 conv over 6 channels as a 16-tap conv on the 32-channel
     space-to-depth layout the fused render+pack writes (grid 83 for 160 crops)."""
     g = torch.Generator().manual_seed(9)
