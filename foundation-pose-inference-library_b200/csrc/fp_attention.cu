@@ -36,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <atomic>
 #include <cstdint>
 #include <string>
 #include <type_traits>
@@ -510,15 +511,15 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
 
 template <typename T>
 cudaError_t launch(const net::AttnArgs& a, int layers, int n_seq, cudaStream_t s) {
-  static int attr_mask = 0;
+  static std::atomic<int> attr_mask{0};  // one bit per device: smem attribute set
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_mask & (1 << dev))) {
+  if (dev < 31 && !(attr_mask.load() & (1 << dev))) {
     const cudaError_t e = cudaFuncSetAttribute(attentionTcKernel<T>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(Geo<T>::kSmem));
     if (e != cudaSuccess) return e;
-    attr_mask |= 1 << dev;
+    attr_mask.fetch_or(1 << dev);
   }
   const int q_tiles = (a.seq_len + kRows - 1) / kRows;
   // Maps over the whole qkv buffer: every plane of every layer, every row of

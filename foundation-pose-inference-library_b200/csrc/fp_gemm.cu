@@ -31,6 +31,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 #include <string>
@@ -826,23 +827,25 @@ bool chooseSlots(uint32_t slot_bytes, uint32_t stage_bytes, int stages_per_chunk
   return best > 0;
 }
 
+// SM count of the first device queried (every GPU of a node is the same
+// part); initialised once, thread-safe.
 int numSms() {
-  static int value = 0;
-  if (value == 0) {
-    int dev = 0;
+  static const int value = [] {
+    int dev = 0, n = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&value, cudaDevAttrMultiProcessorCount, dev);
-  }
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+  }();
   return value;
 }
 
 template <typename T, int BN, int MH>
 int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, size_t smem,
            cudaStream_t stream) {
-  static int attr_mask = 0;
+  static std::atomic<int> attr_mask{0};  // one bit per device: smem attribute set
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_mask & (1 << dev))) {
+  if (dev < 31 && !(attr_mask.load() & (1 << dev))) {
     const cudaError_t e = cudaFuncSetAttribute(gemmKernel<T, BN, MH>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kSmemBytes));
@@ -850,7 +853,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
       cudaGetLastError();
       return fail(std::string("fpk_gemm smem attribute: ") + cudaGetErrorString(e));
     }
-    attr_mask |= 1 << dev;
+    attr_mask.fetch_or(1 << dev);
   }
   const int tiles = pl.m_tiles * pl.n_tiles;
   const int grid = tiles < numSms() ? tiles : numSms();
@@ -863,23 +866,23 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
   return checkLaunch("gemmKernel");
 }
 
-bool g_cta_pairs = true;
+std::atomic<bool> g_cta_pairs{true};
 template <typename T, int BN, int MH>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
                const CUtensorMap& map_a_tail, size_t smem, cudaStream_t stream) {
-  static int attr_mask = 0;
+  static std::atomic<int> attr_mask{0};  // one bit per device: smem attribute set
   static std::mutex mu;
   static std::unordered_map<long long, int> clusters_for;  // (device, smem) -> co-resident pairs
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_mask & (1 << dev))) {
+  if (dev < 31 && !(attr_mask.load() & (1 << dev))) {
     const cudaError_t e = cudaFuncSetAttribute(gemmPairKernel<T, BN, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) {
       cudaGetLastError();
       return fail(std::string("fpk_gemm (pairs) smem attribute: ") + cudaGetErrorString(e));
     }
-    attr_mask |= 1 << dev;
+    attr_mask.fetch_or(1 << dev);
   }
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1031,7 +1034,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   const int pair_mh = bn == 256 ? 1 : 2;
   const int pair_planes = pl.cw * esize / 16;
   const int pair_boxes = (pair_mh * kBlockM + (mx - mn) + 127) / 128;  // row-run boxes per window plane
-  if (g_cta_pairs && (bn == 256 || (bn <= 128 && d.cout == bn)) && pair_boxes <= 4 &&
+  if (g_cta_pairs.load() && (bn == 256 || (bn <= 128 && d.cout == bn)) && pair_boxes <= 4 &&
       (pair_boxes == 1 || pair_boxes * pair_planes <= 32)) {
     // For 1x1 layers the weight order does not depend on the chunk width
     // (k' = channel), so wider windows (fewer activation barriers per MMA) are
@@ -1130,7 +1133,5 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
 }
 
 extern "C" int fpk_gemm_set_cta_pairs(int enable) {
-  const int prev = fpb::gemm::g_cta_pairs ? 1 : 0;
-  fpb::gemm::g_cta_pairs = enable != 0;
-  return prev;
+  return fpb::gemm::g_cta_pairs.exchange(enable != 0) ? 1 : 0;
 }

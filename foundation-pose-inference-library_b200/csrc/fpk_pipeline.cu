@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -1056,16 +1057,15 @@ size_t renderSmemBytes(int rows_per_band, int width) {
 // Largest dynamic shared memory a render CTA may request on the current
 // device: the opt-in per-block limit minus the kernel's static shared memory.
 int maxDynamicSmem() {
-  static int value = -1;
-  if (value < 0) {
+  static const int value = [] {  // initialised once, thread-safe
     int dev = 0;
     cudaGetDevice(&dev);
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa{};
     const size_t stat = cudaFuncGetAttributes(&fa, rasterKernel) == cudaSuccess ? fa.sharedSizeBytes : 1024;
-    value = optin - static_cast<int>(stat) - 256;
-  }
+    return optin - static_cast<int>(stat) - 256;
+  }();
   return value;
 }
 
@@ -1109,17 +1109,17 @@ int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStr
   if (planBands(&a.p, a.n, &rows, &nb) != 0) return 1;
   a.rows_per_band = rows;
   const size_t smem = renderSmemBytes(rows, a.p.input_width);
-  static int attr_done_mask = 0;  // one bit per device
+  static std::atomic<int> attr_done_mask{0};  // one bit per device: smem attribute set
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_done_mask & (1 << dev))) {
+  if (dev < 31 && !(attr_done_mask.load() & (1 << dev))) {
     const cudaError_t e =
         cudaFuncSetAttribute(rasterKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxDynamicSmem());
     if (e != cudaSuccess) {
       cudaGetLastError();
       return fail(std::string("rasterKernel smem attribute: ") + cudaGetErrorString(e));
     }
-    attr_done_mask |= 1 << dev;
+    attr_done_mask.fetch_or(1 << dev);
   }
   const RenderWorkspace ws(a.n, a.mesh.n_vertices, a.p.input_width, a.p.input_height);
   void* mem = workspace;
