@@ -124,3 +124,19 @@ def test_fpk_param_defaults():
     assert p.erosion_radius == 2 and p.bilateral_radius == 2
     assert abs(p.depth_min - 0.001) < 1e-9 and abs(p.rotation_normalizer_rad - 0.34906585) < 1e-7
     assert abs(p.ambient_weight - 0.8) < 1e-7 and abs(p.diffuse_weight - 0.5) < 1e-7
+
+
+def test_cta_pair_switch_round_trip():
+    """fpk_gemm_set_cta_pairs returns the previous setting (pairs on by
+    default) and touches no device state, so it is callable without a GPU."""
+    from fp_b200.kernels import FpkLibrary
+
+    fpk = FpkLibrary(LIB)
+    first = fpk.lib.fpk_gemm_set_cta_pairs(0)
+    try:
+        assert first == 1
+        assert fpk.lib.fpk_gemm_set_cta_pairs(0) == 0
+        assert fpk.lib.fpk_gemm_set_cta_pairs(7) == 0  # any non-zero value enables
+        assert fpk.lib.fpk_gemm_set_cta_pairs(1) == 1
+    finally:
+        fpk.lib.fpk_gemm_set_cta_pairs(first)
