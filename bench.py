@@ -281,9 +281,9 @@ def main() -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300))
 
-    import foundation_pose_nvidia as fpn
-    from foundation_pose_nvidia.bindings import CreateOptions, PoseResult
+    from fp_b200.capi import SCORE_FEATURE_DIM, Api, FP_PRECISION_FP16, image_view
     from fp_b200.kernels import FpkLibrary
+    from fp_b200.sharded import gather_shards, shard_range
 
     work = Path(tempfile.mkdtemp(prefix=f"fpbench_{rank}_"))
     # Every rank builds the same seeded scene: at N > 1 the ranks share one
@@ -291,55 +291,41 @@ def main() -> None:
     mesh, obj, refine, score, gt = build_scene(work, seed=args.seed)
     rgb, depth, mask = render_frame(mesh, gt)
 
-    lib = fpn.load_library(print_build_info=False)
+    api = Api()
     fpk = FpkLibrary()
     fpk.lib.fpk_profile_enable.argtypes = [C.c_int]
     fpk.lib.fpk_profile_read.argtypes = [C.c_void_p] * 4
-    cfg = lib.default_config()
-    cfg.n_hypotheses, cfg.n_refine_iters, cfg.batch_size = N_HYP, N_ITERS, N_HYP
-    cfg.tensorrt_precision = FP16
-    cfg.capture_cuda_graph = 1 if args.graph else 0
-    cfg.max_image_width, cfg.max_image_height = W, H
-    strs = [str(obj).encode(), str(refine).encode(), str(score).encode(), str(work).encode()]
-    opts = CreateOptions(strs[0], local, 1.0, strs[1], strs[2], strs[3])
-    err = C.create_string_buffer(2048)
-    h = lib.cdll.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
-    if not h:
-        raise SystemExit(f"fp_create failed: {err.value.decode()}")
-    if lib.cdll.fp_prepare(h, N_HYP, err, len(err)) != 0:
-        raise SystemExit(f"fp_prepare failed: {err.value.decode()}")
+    cfg = api.default_config(n_hypotheses=N_HYP, n_refine_iters=N_ITERS, batch_size=N_HYP,
+                             tensorrt_precision=FP_PRECISION_FP16, capture_cuda_graph=args.graph,
+                             max_image_width=W, max_image_height=H)
+    opts = Api.options(obj, refine, score, local, work)
+    h = api.create(opts, cfg)
+    api.prepare(h, N_HYP)
 
     dev = torch.device("cuda", local)
     d_rgb, d_depth, d_mask = (torch.from_numpy(x).to(dev) for x in (rgb, depth, mask))
     p_rgb, p_depth, p_mask = (torch.from_numpy(x).pin_memory() for x in (rgb, depth, mask))
     K = np.array([[600, 0, 320], [0, 600, 240], [0, 0, 1]], np.float32)
-    dev_view = fpn.RgbdFrame(d_rgb, d_depth, K, d_mask).to_image_view(with_mask=True)
-    host_view = fpn.RgbdFrame(p_rgb.numpy(), p_depth.numpy(), K, p_mask.numpy()).to_image_view(with_mask=True)
-    result = PoseResult()
-    from foundation_pose_nvidia.core.sharded import FEATURE_DIM, gather_shards, shard_range
-
+    dev_view = image_view(d_rgb, d_depth, K, d_mask)
+    host_view = image_view(p_rgb, p_depth, K, p_mask)
     shard_begin, shard_count = shard_range(N_HYP, world, rank)
     per = -(-N_HYP // world)
-    feats = torch.zeros((per, FEATURE_DIM), dtype=torch.float32, device=dev)
+    feats = torch.zeros((per, SCORE_FEATURE_DIM), dtype=torch.float32, device=dev)
     shard_poses = torch.zeros((per, 16), dtype=torch.float32, device=dev)
+    last = {}
 
     def register(v, handle=None):
         hh = h if handle is None else handle
         if world == 1:
-            if lib.cdll.fp_register_frame(hh, C.byref(v), -1, -1, C.byref(result), err, len(err)) != 0:
-                raise SystemExit(f"fp_register_frame failed: {err.value.decode()}")
+            last["pose"], _ = api.register(hh, v)
             return
         # Sharded register: local shard, NCCL all-gather of ScoreNet features
         # and refined poses, cross-hypothesis head + arg-max on every rank.
-        if lib.cdll.fp_register_shard_begin(hh, C.byref(v), -1, N_HYP, shard_begin, shard_count, feats.data_ptr(),
-                                            shard_poses.data_ptr(), err, len(err)) != 0:
-            raise SystemExit(f"fp_register_shard_begin failed: {err.value.decode()}")
+        api.shard_begin(hh, v, -1, N_HYP, shard_begin, shard_count, feats.data_ptr(), shard_poses.data_ptr())
         all_f = gather_shards(feats, N_HYP)
         all_p = gather_shards(shard_poses, N_HYP)
         torch.cuda.synchronize(dev)
-        if lib.cdll.fp_register_shard_finish(hh, all_f.data_ptr(), all_p.data_ptr(), N_HYP, C.byref(result), err,
-                                             len(err)) != 0:
-            raise SystemExit(f"fp_register_shard_finish failed: {err.value.decode()}")
+        last["pose"], _ = api.shard_finish(hh, all_f.data_ptr(), all_p.data_ptr(), N_HYP)
 
     from fp_b200.dist_utils import barrier
     from fp_b200.dist_utils import max_over_ranks as _max
@@ -366,7 +352,7 @@ def main() -> None:
     clocks = sampler.stop()
     ms_per_step = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     value = N_HYP / (ms_per_step / 1000.0)  # one 252-hypothesis register per step, across all ranks
-    pose_dev = np.array(result.pose_row_major, np.float32).reshape(4, 4)
+    pose_dev = last["pose"].copy()
 
     # End-to-end: pinned host buffers, H2D of the frame and D2H of the pose inside each step.
     e2e_steps = args.steps if args.e2e_steps is None else args.e2e_steps
@@ -384,7 +370,7 @@ def main() -> None:
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(e2.elapsed_time(e3) / e2e_steps)
-        pose_host = np.array(result.pose_row_major, np.float32).reshape(4, 4)
+        pose_host = last["pose"].copy()
 
     # Stage split, GEMM roofline and launch counts: CUDA events per stage on
     # eager registers (a replayed graph hides its launches from the host-side
@@ -393,12 +379,10 @@ def main() -> None:
     prof_steps = 2
     hp = h
     if args.graph:
-        cfg_eager = lib.default_config()
-        C.memmove(C.byref(cfg_eager), C.byref(cfg), C.sizeof(cfg))
-        cfg_eager.capture_cuda_graph = 0
-        hp = lib.cdll.fp_create(C.byref(opts), C.byref(cfg_eager), err, len(err))
-        if not hp:
-            raise SystemExit(f"fp_create (profiling estimator) failed: {err.value.decode()}")
+        cfg_eager = api.default_config(n_hypotheses=N_HYP, n_refine_iters=N_ITERS, batch_size=N_HYP,
+                                       tensorrt_precision=FP_PRECISION_FP16, capture_cuda_graph=False,
+                                       max_image_width=W, max_image_height=H)
+        hp = api.create(opts, cfg_eager)
     register(dev_view, hp)
     torch.cuda.synchronize()
     fpk.lib.fpk_profile_reset()
@@ -413,23 +397,22 @@ def main() -> None:
     launches = (C.c_longlong * 5)()
     fpk.lib.fpk_profile_read(ms_tot, work_tot, timed, launches)
     if hp != h:
-        lib.cdll.fp_destroy(hp)
+        api.destroy(hp)
     launches_per_register = sum(launches[i] for i in range(5)) / prof_steps
 
     # Track rate on the same estimator (B=1, 2 iterations), device-resident frame.
-    track_view = fpn.RgbdFrame(d_rgb, d_depth, K).to_image_view(with_mask=False)
+    track_view = image_view(d_rgb, d_depth, K)
     track_hz = None
     if args.track_frames > 0:
         for _ in range(5):
-            lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err))
+            api.track(h, track_view)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for _ in range(args.track_frames):
-            if lib.cdll.fp_track_frame(h, C.byref(track_view), -1, C.byref(result), err, len(err)) != 0:
-                raise SystemExit(f"fp_track_frame failed: {err.value.decode()}")
+            api.track(h, track_view)
         torch.cuda.synchronize()
         track_hz = args.track_frames / (time.perf_counter() - t0)
-    lib.cdll.fp_destroy(h)
+    api.destroy(h)
 
     if rank == 0:
         pk = peaks()

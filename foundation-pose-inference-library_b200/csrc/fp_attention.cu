@@ -511,16 +511,12 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
 
 template <typename T>
 cudaError_t launch(const net::AttnArgs& a, int layers, int n_seq, cudaStream_t s) {
-  static std::atomic<int> attr_mask{0};  // one bit per device: smem attribute set
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_mask.load() & (1 << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(attentionTcKernel<T>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(Geo<T>::kSmem));
-    if (e != cudaSuccess) return e;
-    attr_mask.fetch_or(1 << dev);
-  }
+  static DeviceOnce smem_attr;
+  const cudaError_t ae = smem_attr.run([] {
+    return cudaFuncSetAttribute(attentionTcKernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(Geo<T>::kSmem));
+  });
+  if (ae != cudaSuccess) return ae;
   const int q_tiles = (a.seq_len + kRows - 1) / kRows;
   // Maps over the whole qkv buffer: every plane of every layer, every row of
   // every sequence; the kernel indexes blocks by (row, first plane).

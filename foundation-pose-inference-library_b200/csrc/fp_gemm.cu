@@ -827,33 +827,27 @@ bool chooseSlots(uint32_t slot_bytes, uint32_t stage_bytes, int stages_per_chunk
   return best > 0;
 }
 
-// SM count of the first device queried (every GPU of a node is the same
-// part); initialised once, thread-safe.
+// SM count of the current device (cached per device).
 int numSms() {
-  static const int value = [] {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
+  static DeviceValue cache;
+  return cache.get([](int dev) {
+    int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     return n > 0 ? n : 148;
-  }();
-  return value;
+  });
 }
 
 template <typename T, int BN, int MH>
 int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, size_t smem,
            cudaStream_t stream) {
-  static std::atomic<int> attr_mask{0};  // one bit per device: smem attribute set
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_mask.load() & (1 << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(gemmKernel<T, BN, MH>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return fail(std::string("fpk_gemm smem attribute: ") + cudaGetErrorString(e));
-    }
-    attr_mask.fetch_or(1 << dev);
+  static DeviceOnce smem_attr;
+  const cudaError_t ae = smem_attr.run([] {
+    return cudaFuncSetAttribute(gemmKernel<T, BN, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kSmemBytes));
+  });
+  if (ae != cudaSuccess) {
+    cudaGetLastError();
+    return fail(std::string("fpk_gemm smem attribute: ") + cudaGetErrorString(ae));
   }
   const int tiles = pl.m_tiles * pl.n_tiles;
   const int grid = tiles < numSms() ? tiles : numSms();
@@ -870,19 +864,17 @@ std::atomic<bool> g_cta_pairs{true};
 template <typename T, int BN, int MH>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
                const CUtensorMap& map_a_tail, size_t smem, cudaStream_t stream) {
-  static std::atomic<int> attr_mask{0};  // one bit per device: smem attribute set
+  static DeviceOnce smem_attr;
   static std::mutex mu;
   static std::unordered_map<long long, int> clusters_for;  // (device, smem) -> co-resident pairs
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_mask.load() & (1 << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(gemmPairKernel<T, BN, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return fail(std::string("fpk_gemm (pairs) smem attribute: ") + cudaGetErrorString(e));
-    }
-    attr_mask.fetch_or(1 << dev);
+  const int dev = currentDevice();
+  const cudaError_t ae = smem_attr.run([] {
+    return cudaFuncSetAttribute(gemmPairKernel<T, BN, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kSmemBytes));
+  });
+  if (ae != cudaSuccess) {
+    cudaGetLastError();
+    return fail(std::string("fpk_gemm (pairs) smem attribute: ") + cudaGetErrorString(ae));
   }
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -8,13 +8,19 @@
 // arena. They can pass in the frame and receive the translation, but cannot let
 // this library cudaMalloc the scratch the chain needs. Here that scratch (the
 // filtered depth map and the 65,536-bin depth histogram) lives in fixed-size
-// device arrays that exist for as long as the library is loaded, on every GPU
-// that loads it: MaxPixels * 4 bytes + 65,544 * 4 bytes, about 3.8 MiB.
+// device arrays of this library's module, on every GPU that uses it:
+// MaxPixels * 4 bytes + 65,544 * 4 bytes, about 3.8 MiB, held until exit.
 //
 // Host code cannot use the arrays' names as device addresses (in host code the
 // name is a host-side stand-in), so the first call on each device looks the
 // addresses up with cudaGetSymbolAddress while that device is current and
-// caches them. That first call should happen before any stream capture.
+// caches them. With CUDA's default lazy module loading, that first lookup is
+// also when the driver loads the module on the device and sets the arrays'
+// memory aside, so the first call on each device is the one that may take
+// device memory: make one warm-up call per device at start-up, before the
+// footprint is frozen and before any stream capture (or run with
+// CUDA_MODULE_LOADING=EAGER, which reserves the arrays when the library's
+// module is loaded).
 // Every call reuses the same arrays: the histogram is cleared at the start of
 // each call, and calls that overlap on the GPU (different streams, or several
 // host threads on one device) race on the arrays and must be serialised by

@@ -1057,16 +1057,14 @@ size_t renderSmemBytes(int rows_per_band, int width) {
 // Largest dynamic shared memory a render CTA may request on the current
 // device: the opt-in per-block limit minus the kernel's static shared memory.
 int maxDynamicSmem() {
-  static const int value = [] {  // initialised once, thread-safe
-    int dev = 0;
-    cudaGetDevice(&dev);
+  static DeviceValue cache;
+  return cache.get([](int dev) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa{};
     const size_t stat = cudaFuncGetAttributes(&fa, rasterKernel) == cudaSuccess ? fa.sharedSizeBytes : 1024;
     return optin - static_cast<int>(stat) - 256;
-  }();
-  return value;
+  });
 }
 
 // Rows per band: the whole crop when its z-buffer fits in shared memory; for
@@ -1109,17 +1107,12 @@ int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStr
   if (planBands(&a.p, a.n, &rows, &nb) != 0) return 1;
   a.rows_per_band = rows;
   const size_t smem = renderSmemBytes(rows, a.p.input_width);
-  static std::atomic<int> attr_done_mask{0};  // one bit per device: smem attribute set
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 31 && !(attr_done_mask.load() & (1 << dev))) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(rasterKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxDynamicSmem());
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return fail(std::string("rasterKernel smem attribute: ") + cudaGetErrorString(e));
-    }
-    attr_done_mask.fetch_or(1 << dev);
+  static DeviceOnce smem_attr;
+  const cudaError_t ae = smem_attr.run(
+      [] { return cudaFuncSetAttribute(rasterKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxDynamicSmem()); });
+  if (ae != cudaSuccess) {
+    cudaGetLastError();
+    return fail(std::string("rasterKernel smem attribute: ") + cudaGetErrorString(ae));
   }
   const RenderWorkspace ws(a.n, a.mesh.n_vertices, a.p.input_width, a.p.input_height);
   void* mem = workspace;

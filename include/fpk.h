@@ -257,9 +257,13 @@ FP_API int fpk_net_error(fpk_net_t* net, int* host_flag);
  * filtered depth and the depth histogram live in fixed device arrays built
  * into the library (about 3.8 MiB on every GPU that loads it, until exit).
  * Frames larger than FPK_NOALLOC_MAX_PIXELS (1280x720) are rejected with an
- * error. The first call on a device looks up the arrays' device addresses and
- * should come before any stream capture. All calls share the arrays: calls that
- * overlap on the GPU race and must be serialised by the caller. */
+ * error. The first call on a device looks up the arrays' device addresses;
+ * under CUDA's default lazy module loading that is also when the driver sets
+ * the arrays' memory aside on that device, so make one warm-up call per device
+ * at start-up, before the memory footprint is frozen and before any stream
+ * capture (CUDA_MODULE_LOADING=EAGER reserves them at library load instead).
+ * All calls share the arrays: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
 #define FPK_NOALLOC_MAX_PIXELS (1280 * 720)
 FP_API int fpk_initial_translation_noalloc(const float* depth_raw, const uint8_t* mask, int width,
                                            int height, fpk_intrinsics_t k, const fpk_params_t* p,

@@ -29,25 +29,21 @@ def main() -> None:
     ap.add_argument("--scene-seed", type=int, default=-1)
     args = ap.parse_args()
 
-    import foundation_pose_nvidia as fpn
-    from foundation_pose_nvidia.bindings import CreateOptions, PoseResult
+    from fp_b200.capi import Api, FpError, image_view
 
-    lib = fpn.load_library(print_build_info=False)
+    api = Api()
     plugin = C.CDLL(args.plugin) if args.plugin else None
     if args.renderer:
         os.environ["FP_RENDERER"] = args.renderer
     else:
         os.environ.pop("FP_RENDERER", None)
-    cfg = lib.default_config()
-    cfg.n_hypotheses = args.n_hyp
-    cfg.batch_size = args.n_hyp
-    cfg.tensorrt_precision = 2  # FP16
-    cfg.max_image_width, cfg.max_image_height = 640, 480
-    strings = [args.obj.encode(), args.refine.encode(), args.score.encode(), args.workdir.encode()]
-    opts = CreateOptions(strings[0], 0, 1.0, strings[1], strings[2], strings[3])
-    err = C.create_string_buffer(2048)
-    h = lib.cdll.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
-    out = {"created": bool(h), "error": err.value.decode()}
+    cfg = api.default_config(n_hypotheses=args.n_hyp, batch_size=args.n_hyp, tensorrt_precision=2,  # FP16
+                             max_image_width=640, max_image_height=480)
+    try:
+        h, error = api.create(Api.options(args.obj, args.refine, args.score, 0, args.workdir), cfg), ""
+    except FpError as e:
+        h, error = None, str(e)
+    out = {"created": bool(h), "error": error}
     if plugin is not None and hasattr(plugin, "fp_test_plugin_created"):
         out.update(factory_calls=plugin.fp_test_plugin_created(), device_id=plugin.fp_test_plugin_device_id(),
                    max_batch=plugin.fp_test_plugin_max_batch())
@@ -56,15 +52,12 @@ def main() -> None:
         from scene_util import make_scene
 
         scene = make_scene(Oracle(), "ellipsoid", seed=args.scene_seed)
-        view = fpn.RgbdFrame(scene.rgb, scene.depth, scene.K, scene.mask).to_image_view(with_mask=True)
-        res = PoseResult()
-        rc = lib.cdll.fp_register_frame(h, C.byref(view), 2, -1, C.byref(res), err, len(err))
-        out.update(register_rc=rc, register_error=err.value.decode(), pose=list(res.pose_row_major),
-                   score=float(res.score))
+        r = api.register_frame(h, image_view(scene.rgb, scene.depth, scene.K, scene.mask), 2, -1)
+        out.update(register_rc=r.rc, register_error=r.error, pose=r.pose.reshape(-1).tolist(), score=r.score)
         if plugin is not None and hasattr(plugin, "fp_test_plugin_render_calls"):
             out["render_calls"] = plugin.fp_test_plugin_render_calls()
     if h:
-        lib.cdll.fp_destroy(h)
+        api.destroy(h)
     print(json.dumps(out))
 
 

@@ -19,8 +19,7 @@ import pytest
 
 torch = pytest.importorskip("torch")
 
-import foundation_pose_nvidia as fpn  # noqa: E402
-from foundation_pose_nvidia.bindings import CreateOptions, ImageView, PoseResult  # noqa: E402
+from fp_b200.capi import Api, FpError, image_view  # noqa: E402
 from fp_b200.weights import make_default_packs, read_pack  # noqa: E402
 from oracle_lib import REF_GPU_SO, RefGpu  # noqa: E402
 from scene_util import make_scene, write_obj  # noqa: E402
@@ -39,25 +38,22 @@ def env(tmp_path_factory, oracle):
     scene = make_scene(oracle, "ellipsoid", seed=4)
     obj = d / "object.obj"
     write_obj(obj, scene.verts, scene.faces, scene.colors_u8)
-    lib = fpn.load_library(print_build_info=False)
+    lib = Api()
     return dict(dir=d, refine=refine, score=score, scene=scene, obj=obj, lib=lib)
 
 
+def config(env, n_hyp=42, batch=None, precision=FP16, graph=False, **kw):
+    return env["lib"].default_config(n_hypotheses=n_hyp, tensorrt_precision=precision, max_image_width=640,
+                                     max_image_height=480, batch_size=batch or n_hyp,
+                                     capture_cuda_graph=graph, **kw)
+
+
+def options(env, device_id=0, obj=None):
+    return Api.options(obj or env["obj"], env["refine"], env["score"], device_id, env["dir"])
+
+
 def create(env, n_hyp=42, batch=None, precision=FP16, graph=False, device_id=0):
-    lib = env["lib"]
-    cfg = lib.default_config()
-    cfg.n_hypotheses = n_hyp
-    cfg.tensorrt_precision = precision
-    cfg.max_image_width, cfg.max_image_height = 640, 480
-    cfg.batch_size = batch or n_hyp
-    cfg.capture_cuda_graph = 1 if graph else 0
-    strings = [str(env["obj"]).encode(), str(env["refine"]).encode(), str(env["score"]).encode(),
-               str(env["dir"]).encode()]
-    opts = CreateOptions(strings[0], device_id, 1.0, strings[1], strings[2], strings[3])
-    err = C.create_string_buffer(1024)
-    h = lib.cdll.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
-    assert h, err.value.decode()
-    return h, strings
+    return env["lib"].create(options(env, device_id), config(env, n_hyp, batch, precision, graph)), None
 
 
 def view(scene, device=False, mask=True):
@@ -65,23 +61,18 @@ def view(scene, device=False, mask=True):
         rgb = torch.from_numpy(scene.rgb).cuda()
         depth = torch.from_numpy(scene.depth).cuda()
         m = torch.from_numpy(scene.mask).cuda() if mask else None
-        return fpn.RgbdFrame(rgb, depth, scene.K, m).to_image_view(with_mask=mask)
-    return fpn.RgbdFrame(scene.rgb, scene.depth, scene.K, scene.mask if mask else None).to_image_view(
-        with_mask=mask)
+        return image_view(rgb, depth, scene.K, m)
+    return image_view(scene.rgb, scene.depth, scene.K, scene.mask if mask else None)
 
 
 def register(lib, h, v, n_refine=2, n_hyp=-1):
-    res = PoseResult()
-    err = C.create_string_buffer(1024)
-    rc = lib.cdll.fp_register_frame(h, C.byref(v), n_refine, n_hyp, C.byref(res), err, len(err))
-    return rc, np.array(res.pose_row_major, np.float32).reshape(4, 4), res.score, err.value.decode()
+    r = lib.register_frame(h, v, n_refine, n_hyp)
+    return r.rc, r.pose, r.score, r.error
 
 
 def track(lib, h, v, n_refine=2):
-    res = PoseResult()
-    err = C.create_string_buffer(1024)
-    rc = lib.cdll.fp_track_frame(h, C.byref(v), n_refine, C.byref(res), err, len(err))
-    return rc, np.array(res.pose_row_major, np.float32).reshape(4, 4), res.score, err.value.decode()
+    r = lib.track_frame(h, v, n_refine)
+    return r.rc, r.pose, r.score, r.error
 
 
 def rot_err_deg(a, b):
@@ -102,45 +93,40 @@ def test_register_track_host_device_identical(env):
     rc, tpose_h, tscore, err = track(lib, h, view(scene, mask=False))
     assert rc == 0, err and tscore == 1.0
     assert tscore == 1.0
-    lib.cdll.fp_destroy(h)
+    lib.destroy(h)
     h2, _ = create(env)
     assert register(lib, h2, view(scene))[0] == 0
     rc, tpose_d, _, err = track(lib, h2, view(scene, device=True, mask=False))
     assert rc == 0, err
     assert np.array_equal(tpose_h, tpose_d)
-    lib.cdll.fp_destroy(h2)
+    lib.destroy(h2)
 
 
 def test_register_errors(env):
     lib, scene = env["lib"], env["scene"]
     # The built-in networks reject a micro-batch that does not divide the
     # hypothesis count at construction, as the reference's runner does.
-    lib_err = C.create_string_buffer(1024)
-    cfg = lib.default_config()
-    cfg.n_hypotheses, cfg.batch_size, cfg.tensorrt_precision = 42, 20, FP16
-    s = [str(env["obj"]).encode(), str(env["refine"]).encode(), str(env["score"]).encode()]
-    opts = CreateOptions(s[0], 0, 1.0, s[1], s[2], None)
-    assert not lib.cdll.fp_create(C.byref(opts), C.byref(cfg), lib_err, len(lib_err))
-    assert "must be divisible by effective_bs" in lib_err.value.decode()
+    with pytest.raises(FpError, match="must be divisible by effective_bs"):
+        lib.create(options(env), config(env, n_hyp=42, batch=20))
     h, _ = create(env, n_hyp=42, batch=21)
     rc, _, _, err = register(lib, h, view(scene), n_hyp=30)
     assert rc != 0 and "must be divisible by batch_size" in err
     rc, _, _, err = track(lib, h, view(scene, mask=False))
     assert rc != 0 and "registerFrame before trackFrame" in err
-    lib.cdll.fp_destroy(h)
+    lib.destroy(h)
     h, _ = create(env, n_hyp=42, batch=21, graph=True)
     rc, _, _, err = register(lib, h, view(scene))
     assert rc != 0 and "capture_cuda_graph is not supported" in err
-    lib.cdll.fp_destroy(h)
+    lib.destroy(h)
     h, _ = create(env, n_hyp=42)
-    v = fpn.RgbdFrame(scene.rgb, scene.depth, scene.K, scene.mask).to_image_view(with_mask=False)
+    v = image_view(scene.rgb, scene.depth, scene.K, None)
     rc, _, _, err = register(lib, h, v)
     assert rc != 0 and "mask pointers are required" in err
-    big = fpn.RgbdFrame(np.zeros((481, 640, 3), np.uint8), np.zeros((481, 640), np.float32), scene.K,
-                        np.zeros((481, 640), np.uint8)).to_image_view(with_mask=True)
+    big = image_view(np.zeros((481, 640, 3), np.uint8), np.zeros((481, 640), np.float32), scene.K,
+                     np.zeros((481, 640), np.uint8))
     rc, _, _, err = register(lib, h, big)
     assert rc != 0 and "max_image_width/max_image_height" in err
-    lib.cdll.fp_destroy(h)
+    lib.destroy(h)
 
 
 def test_micro_batched_register_matches_full_batch(env):
@@ -152,8 +138,8 @@ def test_micro_batched_register_matches_full_batch(env):
     r2 = register(lib, h2, view(scene))
     assert r1[0] == 0 and r2[0] == 0
     assert np.array_equal(r1[1], r2[1]) and r1[2] == r2[2]
-    lib.cdll.fp_destroy(h1)
-    lib.cdll.fp_destroy(h2)
+    lib.destroy(h1)
+    lib.destroy(h2)
 
 
 def test_cuda_graph_register_matches_eager(env):
@@ -165,39 +151,24 @@ def test_cuda_graph_register_matches_eager(env):
     r3 = register(lib, h2, view(scene))
     assert r1[0] == 0 and r2[0] == 0 and r3[0] == 0, (r2[3], r3[3])
     assert np.array_equal(r1[1], r2[1]) and np.array_equal(r2[1], r3[1])
-    lib.cdll.fp_destroy(h1)
-    lib.cdll.fp_destroy(h2)
+    lib.destroy(h1)
+    lib.destroy(h2)
 
 
 def test_group_matches_single_and_skips(env):
     lib, scene = env["lib"], env["scene"]
-    lib.bind_group_api(2)
-    cfg = lib.default_config()
-    cfg.n_hypotheses, cfg.tensorrt_precision, cfg.batch_size = 42, FP16, 42
-    cfg.max_image_width, cfg.max_image_height = 640, 480
-    s = [str(env["obj"]).encode(), str(env["refine"]).encode(), str(env["score"]).encode(),
-         str(env["dir"]).encode()]
-    objs = (CreateOptions * 2)(CreateOptions(s[0], 0, 1.0, s[1], s[2], s[3]),
-                               CreateOptions(s[0], 0, 1.0, s[1], s[2], s[3]))
-    err = C.create_string_buffer(1024)
-    g = lib.cdll.fp_group_create(objs, 2, C.byref(cfg), err, len(err))
-    assert g, err.value.decode()
-    assert lib.cdll.fp_group_size(g) == 2
+    g = lib.group_create([options(env), options(env)], config(env, n_hyp=42))
+    assert lib.lib.fp_group_size(g) == 2
     v = view(scene, mask=False)
-    mask = np.ascontiguousarray(scene.mask)
-    masks = (C.POINTER(C.c_uint8) * 2)(mask.ctypes.data_as(C.POINTER(C.c_uint8)), C.POINTER(C.c_uint8)())
-    results = (PoseResult * 2)()
-    statuses = (C.c_int * 2)()
-    rc = lib.cdll.fp_group_register_frame(g, C.byref(v), masks, 2, -1, results, statuses, err, len(err))
-    assert rc == 0, err.value.decode()
-    assert list(statuses) == [0, 2]  # FP_OBJECT_OK, FP_OBJECT_SKIPPED
+    fails, gposes, gscores, statuses, err = lib.group_register(g, v, [scene.mask, None], n_refine=2)
+    assert fails == 0, err
+    assert statuses == [0, 2]  # FP_OBJECT_OK, FP_OBJECT_SKIPPED
     h, _ = create(env, n_hyp=42)
     rc, pose, score, e = register(lib, h, view(scene))
     assert rc == 0, e
-    gpose = np.array(results[0].pose_row_major, np.float32).reshape(4, 4)
-    assert np.abs(gpose - pose).max() < 1e-5 and abs(results[0].score - score) < 1e-5
-    lib.cdll.fp_destroy(h)
-    lib.cdll.fp_group_destroy(g)
+    assert np.abs(gposes[0] - pose).max() < 1e-5 and abs(gscores[0] - score) < 1e-5
+    lib.destroy(h)
+    lib.lib.fp_group_destroy(g)
 
 
 def reference_register(env, oracle, n_hyp, iters):
@@ -232,7 +203,7 @@ def test_register_matches_reference_kernels_and_torch_networks(env, oracle, n_hy
     h, _ = create(env, n_hyp=n_hyp, precision=precision)
     rc, pose, score, err = register(lib, h, view(scene), n_refine=iters)
     assert rc == 0, err
-    lib.cdll.fp_destroy(h)
+    lib.destroy(h)
     ref, poses, scores = reference_register(env, oracle, n_hyp, iters)
     ref_best, ref_score, ref_idx = ref.select_best(poses, scores, scene.center)
     # Un-centred reference poses of every hypothesis; ours must match the one we picked.
@@ -262,13 +233,8 @@ def test_default_config_registers(env):
     cfg = lib.default_config()
     assert cfg.tensorrt_precision == TF32
     cfg.max_image_width, cfg.max_image_height = 640, 480
-    s = [str(env["obj"]).encode(), str(env["refine"]).encode(), str(env["score"]).encode(),
-         str(env["dir"]).encode()]
-    opts = CreateOptions(s[0], 0, 1.0, s[1], s[2], s[3])
-    err = C.create_string_buffer(1024)
-    h = lib.cdll.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
-    assert h, err.value.decode()
+    h = lib.create(options(env), cfg)
     rc, pose, score, e = register(lib, h, view(scene))
     assert rc == 0, e
     assert np.isfinite(pose).all() and np.isfinite(score)
-    lib.cdll.fp_destroy(h)
+    lib.destroy(h)

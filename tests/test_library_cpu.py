@@ -10,9 +10,9 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-import foundation_pose_nvidia as fpn
-from foundation_pose_nvidia.bindings import (Config, CreateOptions, ImageView, PoseResult,
-                                             ReferenceImageView)
+from fp_b200.capi import (Api, fp_config_t as Config, fp_create_options_t as CreateOptions,
+                         fp_image_view_t as ImageView, fp_pose_result_t as PoseResult,
+                         fp_reference_image_view_t as ReferenceImageView)
 
 ROOT = Path(__file__).resolve().parents[1]
 LIB = ROOT / "foundation-pose-inference-library_b200" / "lib" / "libfoundation_pose_nvidia.so"
@@ -30,7 +30,7 @@ def declared_symbols() -> set[str]:
 @pytest.fixture(scope="module")
 def lib():
     assert LIB.is_file(), "library not built"
-    return fpn.load_library(LIB, print_build_info=False)
+    return Api(LIB)
 
 
 def test_every_declared_symbol_is_exported(lib):
@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
                      "fp_synchronize_device", "fp_build_info"}
     assert reference_abi <= names
     for n in sorted(names):
-        assert hasattr(lib.cdll, n), f"{n} declared in include/ but not exported"
+        assert hasattr(lib.lib, n), f"{n} declared in include/ but not exported"
 
 
 def test_struct_layouts_match_reference():
@@ -67,16 +67,6 @@ def test_default_config_matches_reference(lib):
     assert abs(c.model_free_depth_edge_threshold - 0.02) < 1e-7
 
 
-def test_runtime_config_round_trip(lib):
-    rc = fpn.RuntimeConfig(n_hypotheses=42, tensorrt_precision=fpn.Precision.FP16, batch_size=21,
-                           capture_cuda_graph=True)
-    c = rc.to_ctypes(lib)
-    assert (c.n_hypotheses, c.tensorrt_precision, c.batch_size, c.capture_cuda_graph) == (42, 2, 21, 1)
-    back = fpn.RuntimeConfig.from_ctypes(c)
-    assert back.n_hypotheses == 42 and back.tensorrt_precision == fpn.Precision.FP16
-    assert back.n_refine_iters == 5
-
-
 def test_build_info(lib):
     assert "B200" in lib.build_info
 
@@ -86,8 +76,7 @@ def _err():
 
 
 def test_error_paths_without_gpu(lib, tmp_path):
-    L = lib.cdll
-    lib.bind_group_api(1)
+    L = lib.lib
     e = _err()
     assert not L.fp_create(None, None, e, len(e))
     assert e.value.decode() == "cad_path is required"

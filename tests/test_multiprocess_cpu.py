@@ -61,7 +61,7 @@ def test_shard_ranges_cover_hypotheses_in_order():
     from pathlib import Path
 
     sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "foundation-pose-inference-library_b200" / "python"))
-    from foundation_pose_nvidia import shard_range
+    from fp_b200.sharded import shard_range
 
     for n in (1, 7, 42, 252):
         for world in (1, 2, 3, 4, 8):
@@ -83,7 +83,7 @@ def _shard_worker(rank, world, port, n, q):
     from pathlib import Path
 
     sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "foundation-pose-inference-library_b200" / "python"))
-    from foundation_pose_nvidia.core.sharded import gather_shards, shard_range
+    from fp_b200.sharded import gather_shards, shard_range
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
