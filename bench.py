@@ -13,10 +13,17 @@ available offline). One step = one fp_register_frame call through the C ABI.
   roofline  the tensor-core GEMM kernel: algorithmic FLOPs / CUDA-event time
   cpu_baseline  the CPU restatement (oracle) + torch CPU networks, bounded sample
 
-Multi-GPU (torchrun): every rank registers its own frame (replicas, weak
-scaling); timing is the max over ranks. `--impl reference` times the CPU
-implementation of the same path (reference CPU preprocessing from oracle/_ref,
-CPU oracle for render/pack/pose kernels, torch fp32 networks on all host cores).
+  reference_gpu  baseline: the reference's own library (estimator, C ABI,
+          kernels, rasterizer; oracle/_ref/libfpref_full.so) with torch/cuDNN
+          FP16 networks in place of its TensorRT engines, same scene and box
+
+Multi-GPU (torchrun): one 252-hypothesis register is sharded over the ranks
+(contiguous hypothesis ranges, NCCL all-gather of ScoreNet features and poses
+before the cross-hypothesis head): strong scaling, timing is the max over
+ranks. `--impl reference` times the CPU implementation of the same path
+(reference CPU preprocessing from oracle/_ref, CPU oracle for render/pack/pose
+kernels, torch fp32 networks on all host cores). `--kernel gemm|render|refine`
+times one stage alone for tuning and ncu captures.
 """
 from __future__ import annotations
 
@@ -229,6 +236,260 @@ def run_reference_arm(args) -> None:
 
 
 # ---------------------------------------------------------------------------
+# Reference GPU baseline: the reference's own library on the same B200
+# ---------------------------------------------------------------------------
+
+REF_FULL_SO = ROOT / "oracle" / "_ref" / "libfpref_full.so"
+
+
+def reference_gpu_baseline(obj, refine, score, rgb, depth, mask, K, steps: int, warmup: int, n_hyp: int,
+                           iters: int, track_frames: int) -> dict:
+    """BASELINE leg (never the measured product): the reference's estimator,
+    C ABI, pipeline kernels and built-in rasterizer, compiled for sm_100a from
+    its unmodified sources (oracle/_ref/libfpref_full.so), with RefineNet /
+    ScoreNet run as torch/cuDNN FP16 networks on the same weight pack in place
+    of its TensorRT engines (oracle/fp_net_torch.py; TensorRT is not installed).
+    Same scene, same configuration, same timing as the product arm: register
+    with the frame resident on the device, register from pinned host buffers,
+    and track at one hypothesis. Network time is measured inside the runner
+    callbacks with CUDA events on the reference's stream."""
+    if not REF_FULL_SO.is_file():
+        return {"unavailable": "oracle/_ref/libfpref_full.so was not built (make -C oracle ref)"}
+    import torch
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from fp_b200 import capi
+    from fp_b200.weights import read_pack
+    from fp_net_torch import TorchNets, install
+
+    lib = C.CDLL(str(REF_FULL_SO))
+    for name, (res, argt) in capi._SIGNATURES.items():
+        if hasattr(lib, name):
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, argt
+    nets = TorchNets(read_pack(refine)[1], read_pack(score)[1], torch.float16)
+    net_ms = {"total": 0.0, "on": False}
+    events = []
+
+    def timed(fn):
+        def wrapped(*a):
+            stream_ptr = a[-1]
+            ext = torch.cuda.ExternalStream(stream_ptr) if stream_ptr else torch.cuda.current_stream()
+            if net_ms["on"]:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(ext)
+                fn(*a)
+                e1.record(ext)
+                events.append((e0, e1))
+            else:
+                fn(*a)
+        return wrapped
+
+    nets.refine_ptrs, nets.score_ptrs = timed(nets.refine_ptrs), timed(nets.score_ptrs)
+    callbacks = install(lib, nets)  # noqa: F841  (kept alive until the handle is destroyed)
+    cfg = capi.fp_config_t()
+    lib.fp_default_config(C.byref(cfg))
+    cfg.n_hypotheses, cfg.n_refine_iters, cfg.batch_size = n_hyp, iters, n_hyp
+    cfg.tensorrt_precision, cfg.capture_cuda_graph = capi.FP_PRECISION_FP16, 0
+    cfg.max_image_width, cfg.max_image_height = rgb.shape[1], rgb.shape[0]
+    opts = capi.Api.options(obj, refine, score, torch.cuda.current_device(), None)
+    err = C.create_string_buffer(4096)
+    h = lib.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
+    if not h:
+        return {"unavailable": f"reference fp_create failed: {err.value.decode()}"}
+    res = capi.fp_pose_result_t()
+
+    def reg(view):
+        if lib.fp_register_frame(h, C.byref(view), -1, -1, C.byref(res), err, len(err)) != 0:
+            raise RuntimeError(f"reference fp_register_frame: {err.value.decode()}")
+
+    def trk(view):
+        if lib.fp_track_frame(h, C.byref(view), -1, C.byref(res), err, len(err)) != 0:
+            raise RuntimeError(f"reference fp_track_frame: {err.value.decode()}")
+
+    try:
+        if lib.fp_prepare(h, n_hyp, err, len(err)) != 0:
+            return {"unavailable": f"reference fp_prepare failed: {err.value.decode()}"}
+        dev = torch.device("cuda", torch.cuda.current_device())
+        d_rgb, d_depth, d_mask = (torch.from_numpy(x).to(dev) for x in (rgb, depth, mask))
+        p_rgb, p_depth, p_mask = (torch.from_numpy(x).pin_memory() for x in (rgb, depth, mask))
+        dev_view = capi.image_view(d_rgb, d_depth, K, d_mask)
+        host_view = capi.image_view(p_rgb, p_depth, K, p_mask)
+
+        def time_steps(fn, view, n):
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                fn(view)
+            b.record()
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / n
+
+        for _ in range(max(3, warmup)):
+            reg(dev_view)
+        reg_ms = time_steps(reg, dev_view, steps)
+        pose = np.array(res.pose_row_major, np.float32).reshape(4, 4)
+        e2e_ms = time_steps(reg, host_view, steps)
+        net_ms["on"] = True
+        events.clear()
+        prof_ms = time_steps(reg, dev_view, 2)
+        net = sum(e0.elapsed_time(e1) for e0, e1 in events) / 2
+        net_ms["on"] = False
+        track_hz = None
+        if track_frames > 0:
+            tview = capi.image_view(d_rgb, d_depth, K)
+            for _ in range(5):
+                trk(tview)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(track_frames):
+                trk(tview)
+            torch.cuda.synchronize()
+            track_hz = track_frames / (time.perf_counter() - t0)
+    finally:
+        lib.fp_destroy(h)
+    return {"register_ms": reg_ms, "hyp_per_s": n_hyp / (reg_ms / 1000.0), "e2e_register_ms": e2e_ms,
+            "track_hz": track_hz, "network_ms_per_register": net, "other_ms_per_register": prof_ms - net,
+            "pose": pose.reshape(-1).tolist(),
+            "build": "reference estimator + C ABI + cuda_pipeline.cu + builtin_raster_renderer.cu, unmodified, "
+                     "sm_100a (oracle/_ref/libfpref_full.so)",
+            "networks": f"torch {torch.__version__} FP16: channels-last cuDNN convolutions (autotuned), fused SDPA "
+                        "attention, CUDA-graph replay per call site (stand-in for the TensorRT engines, not installed)",
+            "capture_cuda_graph": 0}
+
+
+# ---------------------------------------------------------------------------
+# Single-kernel drivers (--kernel): one hot-path stage on synthetic inputs, for
+# tuning and ncu captures. One JSON line with the CUDA-event time per launch
+# and the rate against the stage's algorithmic work.
+# ---------------------------------------------------------------------------
+
+class _Planar:
+    """KP8 activation buffer with zeroed guard rows (layout in include/fpk.h)."""
+
+    def __init__(self, torch, rows: int, channels: int, dtype):
+        total = (256 + rows + 512 + 15) // 16 * 16
+        self.t = torch.zeros((channels // 8, total, 8), dtype=dtype, device="cuda")
+        self.base = self.t.data_ptr() + 256 * 16
+        self.stride = total * 16
+
+
+def _time_launches(torch, fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def kernel_gemm(args) -> dict:
+    """One 3x3 (or 1x1) implicit-GEMM convolution layer, KP8 planar in and out."""
+    import torch
+
+    from fp_b200.kernels import FPK_DST_SAME, FPK_DTYPE_BF16, FPK_DTYPE_F16, FpkLibrary, GemmDesc, gemm
+
+    fpk = FpkLibrary()
+    fpk.lib.fpk_gemm_set_cta_pairs(args.pairs)
+    dt = torch.float16 if args.kdtype == "f16" else torch.bfloat16
+    g = args.grid
+    valid = g - 1
+    rows = args.batch * g * g
+    a = _Planar(torch, rows, args.cin, dt)
+    a.t.uniform_(-1, 1)
+    out = _Planar(torch, rows, args.cout, dt)
+    taps = [(ky - 1) * g + (kx - 1) for ky in range(3) for kx in range(3)] if args.taps == 9 else [0]
+    w = (torch.randn(args.cout, len(taps) * args.cin, device="cuda") / math.sqrt(len(taps) * args.cin)).to(dt)
+    bias = torch.zeros(args.cout, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d = GemmDesc()
+    d.a, d.a_plane_stride, d.rows, d.cin, d.taps = a.base, a.stride, rows, args.cin, len(taps)
+    for i, o in enumerate(taps):
+        d.tap_off[i] = o
+    d.w, d.cout, d.bias = w.data_ptr(), args.cout, bias.data_ptr()
+    d.relu, d.dst, d.dst_plane_stride, d.dst_mode = 1, out.base, out.stride, FPK_DST_SAME
+    d.img_rows, d.grid_w, d.valid_h, d.valid_w = g * g, g, valid, valid
+    d.img_mod, d.dtype, d.error_flag = 1, FPK_DTYPE_F16 if args.kdtype == "f16" else FPK_DTYPE_BF16, err.data_ptr()
+    ms = _time_launches(torch, lambda: gemm(fpk, d), args.iters)
+    flops = 2.0 * args.batch * valid * valid * args.cout * len(taps) * args.cin
+    return {"kernel": "gemmPairKernel/gemmKernel", "cta_pairs": args.pairs, "batch": args.batch, "cin": args.cin,
+            "cout": args.cout, "grid": g, "taps": len(taps), "ms": ms, "tflops": flops / ms / 1e9,
+            "hbm_bytes": rows * (args.cin + args.cout) * 2, "error_flag": int(err.item())}
+
+
+def kernel_render(args) -> dict:
+    """fpk_render_pack over a batch of hypotheses of a displaced sphere (or the
+    250k-triangle mesh with --faces 250000 --frame 1280x720)."""
+    import torch
+
+    from fp_b200 import synthetic as syn
+    from fp_b200.kernels import FPK_DTYPE_F16, FpkLibrary, Intrinsics, Mesh
+
+    fpk = FpkLibrary()
+    fw, fh = (1280, 720) if args.frame == "1280x720" else (640, 480)
+    K = syn.K_1280 if args.frame == "1280x720" else syn.K_640
+    mesh = syn.dense_mesh(1, args.faces) if args.faces > 60000 else \
+        syn.displaced_sphere(1, n_lat=int(round(args.faces / 400)) + 2, n_lon=200)
+    normals = syn.vertex_normals(mesh.vertices, mesh.faces)
+    rng = np.random.default_rng(0)
+    gt = syn.random_pose(rng, dist=(0.65, 0.75), lateral=0.03)
+    rgb, depth = syn.render_frame_gpu(fpk, mesh, normals, gt, K, fw, fh)
+    dev = "cuda"
+    v = torch.from_numpy(mesh.vertices).to(dev)
+    nr = torch.from_numpy(normals).to(dev)
+    col = torch.from_numpy(mesh.colors.astype(np.float32) / np.float32(255.0)).to(dev)
+    f = torch.from_numpy(mesh.faces).to(dev)
+    m = Mesh(v.data_ptr(), nr.data_ptr(), col.data_ptr(), None, None, f.data_ptr(), v.shape[0], f.shape[0], 0, 0)
+    poses = np.repeat(gt.reshape(1, 16), args.batch, 0).astype(np.float32)
+    poses.reshape(-1, 4, 4)[:, :3, :3] = np.stack([syn.rotation_matrix(rng) for _ in range(args.batch)])
+    P = torch.from_numpy(poses).to(dev)
+    d_rgb, d_depth = torch.from_numpy(rgb).to(dev), torch.from_numpy(depth).to(dev)
+    params = fpk.default_params()
+    k = Intrinsics(float(K[0, 0]), float(K[1, 1]), float(K[0, 2]), float(K[1, 2]))
+    net = _Planar(torch, 2 * args.batch * 83 * 83, 32, torch.float16)
+    boxes = torch.empty((args.batch, 4), device=dev)
+    diam = float(np.linalg.norm(mesh.vertices.max(0) - mesh.vertices.min(0)))
+    ws_bytes = fpk.render_workspace_bytes(args.batch, v.shape[0], params)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+
+    def run():
+        fpk.render_pack(m, P.data_ptr(), args.batch, d_rgb.data_ptr(), d_depth.data_ptr(), fw, fh, k, params, diam,
+                        0.001, FPK_DTYPE_F16, net.base, net.stride, boxes.data_ptr(), workspace=ws.data_ptr(),
+                        workspace_bytes=ws_bytes)
+
+    ms = _time_launches(torch, run, args.iters)
+    px = args.batch * 160 * 160
+    nbytes = v.shape[0] * 36 + f.shape[0] * 12 + fw * fh * 7 + px * 12 * 2
+    return {"kernel": "fpk_render_pack (fp16 stem layout)", "batch": args.batch, "faces": int(f.shape[0]),
+            "frame": args.frame, "ms": ms, "gbs": nbytes / ms / 1e6, "tris_per_s": args.batch * f.shape[0] / ms * 1e3}
+
+
+def kernel_refine(args) -> dict:
+    """One RefineNet forward (all GEMM, attention and LayerNorm launches)."""
+    import torch
+
+    from fp_b200.kernels import FpkLibrary, Networks
+    from fp_b200.weights import make_default_packs
+
+    prec = {"f16": 2, "bf16": 3, "tf32": 1, "f32": 0}[args.kdtype]
+    refine, score = make_default_packs(Path(tempfile.mkdtemp(prefix="fpk_")), seed=0)
+    netw = Networks(FpkLibrary(), refine, score, prec, args.batch)
+    A = torch.rand(args.batch, 6, 160, 160, device="cuda")
+    B = torch.rand(args.batch, 6, 160, 160, device="cuda")
+    t = torch.zeros(args.batch, 3, device="cuda")
+    r = torch.zeros(args.batch, 3, device="cuda")
+    ms = _time_launches(torch, lambda: netw.refine(A.data_ptr(), B.data_ptr(), args.batch, t.data_ptr(),
+                                                   r.data_ptr()), args.iters)
+    return {"kernel": "RefineNet forward", "batch": args.batch, "precision": args.kdtype, "ms": ms,
+            "error_flag": netw.error_flag()}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 
@@ -252,6 +513,8 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--cpu-sample", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
+                    help="skip the reference-library GPU baseline (oracle/_ref/libfpref_full.so + torch networks)")
     ap.add_argument("--track-frames", type=int, default=50)
     ap.add_argument("--e2e-steps", type=int, default=None, help="host-buffer steps (default: --steps)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
@@ -260,7 +523,23 @@ def main() -> None:
     ap.add_argument("--hyp", type=int, default=252,
                     help="hypotheses per register; values other than 252 are for profiling captures only "
                          "(the workload line then names the reduced count)")
+    ap.add_argument("--kernel", choices=["gemm", "render", "refine"], default=None,
+                    help="time one hot-path stage alone (tuning / ncu captures) instead of the register step")
+    ap.add_argument("--batch", type=int, default=128, help="--kernel: images / hypotheses per launch")
+    ap.add_argument("--cin", type=int, default=256)
+    ap.add_argument("--cout", type=int, default=256)
+    ap.add_argument("--grid", type=int, default=41, help="--kernel gemm: padded grid side (41 = 40x40 stage)")
+    ap.add_argument("--taps", type=int, default=9, choices=[1, 9])
+    ap.add_argument("--faces", type=int, default=50000)
+    ap.add_argument("--frame", default="640x480", choices=["640x480", "1280x720"])
+    ap.add_argument("--kdtype", default="f16", choices=["f16", "bf16", "tf32", "f32"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--pairs", type=int, default=1, choices=[0, 1])
     args = ap.parse_args()
+    if args.kernel is not None:
+        fn = {"gemm": kernel_gemm, "render": kernel_render, "refine": kernel_refine}[args.kernel]
+        print(json.dumps(fn(args)), flush=True)
+        return
     global N_HYP, WORKLOAD
     if args.hyp != N_HYP:
         N_HYP = args.hyp
@@ -427,6 +706,17 @@ def main() -> None:
                         "sample": f"{args.cpu_sample} hypotheses x (preprocess + 5 refine + 1 score pass) "
                                   "on the host: reference CPU preprocessDepth, CPU oracle render/pack/pose, "
                                   "torch fp32 networks"}
+        ref_gpu = None
+        if args.reference_gpu and world == 1:
+            ref_gpu = reference_gpu_baseline(obj, refine, score, rgb, depth, mask, K, args.steps, args.warmup, N_HYP,
+                                             N_ITERS, args.track_frames)
+            if "register_ms" in ref_gpu:
+                ref_gpu["speedup_register"] = ref_gpu["register_ms"] / ms_per_step
+                ref_gpu["speedup_register_e2e"] = ref_gpu["e2e_register_ms"] / e2e_ms
+                if track_hz and ref_gpu.get("track_hz"):
+                    ref_gpu["speedup_track"] = track_hz / ref_gpu["track_hz"]
+                ref_pose = np.array(ref_gpu.pop("pose"), np.float32).reshape(4, 4)
+                ref_gpu["pose_dt_mm_vs_product"] = float(np.linalg.norm(ref_pose[:3, 3] - pose_dev[:3, 3]) * 1000)
         line = {
             "metric": METRIC, "value": value, "unit": "hyp/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -440,7 +730,8 @@ def main() -> None:
             "e2e": {"value": N_HYP / (e2e_ms / 1000.0) if e2e_steps > 0 else None, "unit": "hyp/s",
                     "h2d_bytes_per_step": int(rgb.nbytes + depth.nbytes + mask.nbytes),
                     "d2h_bytes_per_step": 72, "register_ms": e2e_ms},
-            "roofline": {"kernel": "gemmKernel (tcgen05 implicit-GEMM conv/linear)", "bound": "tensor",
+            "roofline": {"kernel": "gemmPairKernel / gemmKernel (tcgen05 implicit-GEMM conv/linear, f16 operands; "
+                                   "the measured bf16 cuBLAS peak stands in for the equal f16 peak)", "bound": "tensor",
                          "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s",
                          "frac": (achieved / pk["bf16"]) if achieved else None, "peak_note": pk["note"],
                          "traffic": GEMM_DRAM_BYTES_PER_TFLOP * (gemm_flops / 1e12) / max(1, gemm_n),
@@ -461,6 +752,7 @@ def main() -> None:
             "track_hz": track_hz,
             "clocks": clocks,
             "cpu_baseline": cpu_base,
+            "reference_gpu": ref_gpu,
             "pose_host_equals_device": None if pose_host is None else bool(np.array_equal(pose_dev, pose_host)),
         }
         print(json.dumps(line), flush=True)

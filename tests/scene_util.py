@@ -48,7 +48,23 @@ def make_mesh(kind: str, seed: int = 0) -> syn.MeshData:
         return syn.ellipsoid_mesh(seed, subdivisions=3)
     if kind == "sphere50k":
         return syn.displaced_sphere(seed)
+    if kind == "dense250k":
+        return syn.dense_mesh(seed)
+    if kind == "bigtris":
+        return big_triangle_soup(seed)
     raise ValueError(kind)
+
+
+def big_triangle_soup(seed: int, n: int = 3000, radius: float = 0.05) -> syn.MeshData:
+    """n independent triangles with corners spread over a ball: nearly every
+    triangle covers a large part of the crop, so the rasterizer's list of
+    CTA-shared large triangles (1,024 entries per CTA) overflows and the rest
+    fall back to per-thread rasterization."""
+    rng = np.random.default_rng(seed)
+    v = rng.normal(size=(3 * n, 3))
+    v *= (radius * rng.uniform(0.3, 1.0, size=(3 * n, 1))) / np.linalg.norm(v, axis=1, keepdims=True)
+    f = np.arange(3 * n, dtype=np.int32).reshape(n, 3)
+    return syn.MeshData(v.astype(np.float32), f, rng.integers(0, 256, size=(3 * n, 3), dtype=np.uint8))
 
 
 def make_scene(oracle, kind: str = "ellipsoid_small", seed: int = 0, width: int = 640,

@@ -195,7 +195,7 @@ def reference_register(env, oracle, n_hyp, iters):
 
 
 @pytest.mark.parametrize("n_hyp,iters,precision", [(1, 3, FP16), (42, 2, FP16), (42, 2, TF32),
-                                                   (1, 2, FP32)])
+                                                   (1, 2, FP32), (252, 5, FP16)])
 def test_register_matches_reference_kernels_and_torch_networks(env, oracle, n_hyp, iters, precision):
     if not REF_GPU_SO.is_file():
         pytest.skip("reference GPU build (oracle/_ref) not present")
@@ -224,6 +224,79 @@ def test_register_matches_reference_kernels_and_torch_networks(env, oracle, n_hy
     assert i == ref_idx or scores[ref_idx] - scores[i] <= 1e-3 * max(1.0, abs(scores[ref_idx]))
     tol = 1e-3 if precision in (FP32, TF32) else 1e-2
     assert abs(score - scores[i]) <= tol * max(1.0, abs(scores[i]))
+
+
+REF_FULL_SO = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libfpref_full.so"
+
+
+@pytest.fixture(scope="module")
+def ref_library(env):
+    """The reference's own library (estimator, C ABI, kernels, rasterizer built
+    from its unmodified sources) with torch fp32 networks on the same weights
+    behind its runner seam (oracle/ref_trt_standin.cpp, oracle/fp_net_torch.py)."""
+    if not REF_FULL_SO.is_file():
+        pytest.skip("reference library build (oracle/_ref/libfpref_full.so) not present")
+    from fp_b200 import capi
+    from fp_net_torch import TorchNets, install
+
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    lib = C.CDLL(str(REF_FULL_SO))
+    for name, (res, argt) in capi._SIGNATURES.items():
+        if hasattr(lib, name):
+            getattr(lib, name).restype, getattr(lib, name).argtypes = res, argt
+    nets = TorchNets(read_pack(env["refine"])[1], read_pack(env["score"])[1], torch.float32, graphs=False)
+    last = {}
+    score_ptrs = nets.score_ptrs
+
+    def keep_scores(r, o, s, n, stream):
+        score_ptrs(r, o, s, n, stream)
+        torch.cuda.ExternalStream(stream).synchronize()
+        from fp_net_torch import device_tensor
+
+        last["scores"] = device_tensor(s, (n,)).cpu().numpy()
+
+    nets.score_ptrs = keep_scores
+    cbs = install(lib, nets)
+    return dict(lib=lib, callbacks=cbs, last=last)
+
+
+@pytest.mark.parametrize("n_hyp,iters,precision", [(42, 2, FP16), (252, 5, FP16), (42, 2, TF32)])
+def test_register_matches_reference_library(env, ref_library, n_hyp, iters, precision):
+    """Our fp_register_frame against the reference's own fp_register_frame
+    (its sequencing, kernels and rasterizer; fp32 torch networks in place of
+    TensorRT) on the same frame, mesh file and weights: final pose within
+    1 mm / 0.1 deg. When the reference's own two best scores are closer than
+    the network tolerance, the top-1 is a tie and only the score is compared."""
+    from fp_b200 import capi
+
+    lib, scene = env["lib"], env["scene"]
+    h, _ = create(env, n_hyp=n_hyp, precision=precision)
+    rc, pose, score, err = register(lib, h, view(scene), n_refine=iters)
+    assert rc == 0, err
+    lib.destroy(h)
+    rl = ref_library["lib"]
+    cfg = config(env, n_hyp, None, precision)
+    e = C.create_string_buffer(4096)
+    rh = rl.fp_create(C.byref(options(env)), C.byref(cfg), e, len(e))
+    assert rh, e.value.decode()
+    res = capi.fp_pose_result_t()
+    try:
+        assert rl.fp_register_frame(rh, C.byref(view(scene)), iters, -1, C.byref(res), e, len(e)) == 0, \
+            e.value.decode()
+    finally:
+        rl.fp_destroy(rh)
+    ref_pose = np.array(res.pose_row_major, np.float32).reshape(4, 4)
+    scores = np.sort(ref_library["last"]["scores"])[::-1]
+    tol = 1e-3 if precision in (FP32, TF32) else 1e-2
+    t_err = float(np.linalg.norm(pose[:3, 3] - ref_pose[:3, 3]) * 1000.0)
+    r_err = rot_err_deg(pose, ref_pose)
+    gap = float(scores[0] - scores[1]) / max(1.0, abs(float(scores[0])))
+    print(f"reference library n={n_hyp} precision={precision}: dt={t_err:.4f} mm dR={r_err:.4f} deg, "
+          f"score {score:.6f} vs {res.score:.6f}, reference top-2 gap {gap:.2e}")
+    assert abs(score - res.score) <= tol * max(1.0, abs(res.score))
+    if gap > tol:
+        assert t_err <= 1.0 and r_err <= 0.1
 
 
 def test_default_config_registers(env):

@@ -84,6 +84,25 @@ def test_score_matches_reference(fpk, packs, ref_models, precision):
     net.close()
 
 
+@pytest.mark.parametrize("precision", [FP16, BF16])
+def test_score_matches_reference_at_252(fpk, packs, ref_models, precision):
+    """ScoreNet over the full register batch: the cross-hypothesis attention
+    attends across all 252 hypotheses (reference tensorrt_runner.cu:523-532
+    never micro-batches ScoreNet)."""
+    n = 252
+    A, B = inputs(n, 4)
+    net = Networks(fpk, packs[0], packs[1], precision, max_batch=n)
+    scores = torch.zeros(n, device=DEV)
+    net.score(A.data_ptr(), B.data_ptr(), n, scores.data_ptr())
+    torch.cuda.synchronize()
+    assert net.error_flag() == 0
+    rs = ref_models[1].score(A, B)
+    e = rel_err(scores, rs)
+    print(f"score n=252 precision={precision} rel err {e:.2e} argmax {scores.argmax().item()} vs {rs.argmax().item()}")
+    assert e <= TOL[precision]
+    net.close()
+
+
 def test_refine_batch_independence(fpk, packs):
     """RefineNet is per-hypothesis: a hypothesis gives the same output alone and
     inside a batch (deterministic kernels, no cross-sample reductions)."""
