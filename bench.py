@@ -489,6 +489,40 @@ def kernel_refine(args) -> dict:
             "error_flag": netw.error_flag()}
 
 
+def kernel_track(args) -> dict:
+    """Track at one hypothesis (2 refinement passes) on the benchmark scene:
+    register once, then time --iters track frames; with --frames-graph the
+    refinement passes replay as CUDA graphs (capture_cuda_graph=1)."""
+    import torch
+
+    from fp_b200.capi import FP_PRECISION_FP16, Api, image_view
+
+    prec = {"f16": FP_PRECISION_FP16, "bf16": 3, "tf32": 1, "f32": 0}[args.kdtype]
+    work = Path(tempfile.mkdtemp(prefix="fpk_track_"))
+    mesh, obj, refine, score, gt = build_scene(work, seed=1)
+    rgb, depth, mask = render_frame(mesh, gt)
+    api = Api()
+    cfg = api.default_config(n_hypotheses=N_HYP, batch_size=N_HYP, tensorrt_precision=prec,
+                             capture_cuda_graph=args.graph, max_image_width=W, max_image_height=H)
+    h = api.create(Api.options(obj, refine, score, 0, work), cfg)
+    K = np.array([[600, 0, 320], [0, 600, 240], [0, 0, 1]], np.float32)
+    dev = torch.device("cuda", 0)
+    d_rgb, d_depth, d_mask = (torch.from_numpy(x).to(dev) for x in (rgb, depth, mask))
+    api.register(h, image_view(d_rgb, d_depth, K, d_mask))
+    view = image_view(d_rgb, d_depth, K)
+    for _ in range(5):
+        api.track(h, view)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.iters):
+        api.track(h, view)
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / args.iters
+    api.destroy(h)
+    return {"kernel": "fp_track_frame (B=1, 2 iterations)", "precision": args.kdtype, "graph": bool(args.graph),
+            "ms": dt * 1000.0, "hz": 1.0 / dt}
+
+
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
@@ -523,7 +557,7 @@ def main() -> None:
     ap.add_argument("--hyp", type=int, default=252,
                     help="hypotheses per register; values other than 252 are for profiling captures only "
                          "(the workload line then names the reduced count)")
-    ap.add_argument("--kernel", choices=["gemm", "render", "refine"], default=None,
+    ap.add_argument("--kernel", choices=["gemm", "render", "refine", "track"], default=None,
                     help="time one hot-path stage alone (tuning / ncu captures) instead of the register step")
     ap.add_argument("--batch", type=int, default=128, help="--kernel: images / hypotheses per launch")
     ap.add_argument("--cin", type=int, default=256)
@@ -537,7 +571,7 @@ def main() -> None:
     ap.add_argument("--pairs", type=int, default=1, choices=[0, 1])
     args = ap.parse_args()
     if args.kernel is not None:
-        fn = {"gemm": kernel_gemm, "render": kernel_render, "refine": kernel_refine}[args.kernel]
+        fn = {"gemm": kernel_gemm, "render": kernel_render, "refine": kernel_refine, "track": kernel_track}[args.kernel]
         print(json.dumps(fn(args)), flush=True)
         return
     global N_HYP, WORKLOAD

@@ -3,15 +3,19 @@
 //
 //  * fpk_preprocess   one tiled pass: erode -> bilateral -> (xyz) -> mask stats
 //  * fpk_seed_poses   parallel histogram-median + pose seeding (one CTA)
-//  * fpk_render[_pack] rasterizer with the z-buffer resident in shared memory:
-//                     one CTA per (hypothesis, row band), crop box, triangle
-//                     setup, depth test, resolve, shade and (fused variant)
-//                     crop-warp + pack straight into the network's input layout
+//  * fpk_render[_pack] vertex pass (crop box, clip and pixel position per
+//                     (hypothesis, vertex), z-buffer clear), one raster thread
+//                     per (hypothesis, triangle) with 64-bit depth keys in an
+//                     L2-resident z-buffer, warp-per-triangle pass for large
+//                     triangles, then per-pixel resolve + shade and (fused
+//                     variant) crop-warp + pack straight into the network's
+//                     input layout
 //  * fpk_apply_deltas / fpk_select_best  pose update and arg-max
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <climits>
 #include <atomic>
 #include <cstdint>
@@ -329,16 +333,16 @@ __global__ void cropBoxesKernel(const float* __restrict__ poses, int n, fpk_intr
 }
 
 // ---------------------------------------------------------------------------
-// Rasterizer with a shared-memory z-buffer.
+// Rasterizer: one thread per (hypothesis, triangle), z-buffer resident in L2.
 // ---------------------------------------------------------------------------
 
-// The triangle loop waits on gathers of per-vertex data (L2 latency; the
-// z-buffer leaves little L1), so the CTA runs as many warps as an SM holds at
-// the kernel's register count: 1024 threads (54 registers) render 252
-// hypotheses 29 % faster than 512.
-constexpr int kRenderThreads = 1024;
-constexpr int kBigListCap = 1024;
-constexpr int kBigTriPixels = 64;  // bbox pixel count above which a CTA shares the triangle
+// A triangle thread tests its own bounding-box pixels up to this many pixels.
+// Larger triangles are queued and walked by a whole warp each, so one large
+// triangle never holds the other 31 lanes of its warp (the common triangle of
+// the 50k-250k meshes covers 4-16 bounding-box pixels).
+constexpr int kSmallTriPixels = 32;
+constexpr int kRasterThreads = 256;
+constexpr int kBigTriThreads = 256;
 
 enum class RenderOut { kNhwc = 0, kS2dF32 = 1, kS2dF16 = 2, kS2dBf16 = 3 };
 
@@ -351,7 +355,6 @@ struct RenderArgs {
   fpk_intrinsics_t k;
   fpk_params_t p;
   float diameter;
-  int rows_per_band;
   // kNhwc outputs
   float* out_rgb;
   float* out_xyz;
@@ -364,11 +367,17 @@ struct RenderArgs {
   void* net;
   long long plane_stride;
   int grid_w, grid_h;  // stem space-to-depth grid (83 x 83 for 160 x 160 crops)
-  // Workspace: per (hypothesis, vertex) clip position and pixel position,
-  // and the triangle-id map [n][H][W] (rast rows, bottom-up; 0 = background).
+  // Workspace: per (hypothesis, vertex) clip position and pixel position; the
+  // z-buffer [n][H][W] of packed (depth, triangle + 1) keys, rast rows
+  // bottom-up (all ones = background; 51.6 MB at 252 hypotheses, so it stays
+  // in the 126 MB L2 between the raster and the shading kernels); the queue of
+  // large triangles as (hypothesis, triangle) pairs.
   float4* vclip;
   float2* vscr;
-  int32_t* ids;
+  unsigned long long* zbuf;
+  int* big_count;
+  int2* big_queue;
+  int big_cap;
 };
 
 struct TriSetup {
@@ -708,6 +717,13 @@ __global__ void __launch_bounds__(256) vertexKernel(RenderArgs a) {
     if (a.boxes_out != nullptr && blockIdx.x == 0) reinterpret_cast<float4*>(a.boxes_out)[hyp] = hs.box;
   }
   __syncthreads();
+  // Clear this hypothesis's z-buffer for the raster grid, which starts only
+  // after this grid has completed (the previous call's shading, which reads
+  // the z-buffer, completed before this grid's wait above returned).
+  const int crop_px = a.p.input_width * a.p.input_height;
+  unsigned long long* z = a.zbuf + static_cast<size_t>(hyp) * crop_px;
+  for (int i = blockIdx.x * blockDim.x + tid; i < crop_px; i += gridDim.x * blockDim.x) z[i] = ~0ull;
+  if (hyp == 0 && blockIdx.x == 0 && tid == 0) *a.big_count = 0;
   const int v = blockIdx.x * blockDim.x + tid;
   const int nv = a.mesh.n_vertices;
   if (v >= nv) return;
@@ -719,101 +735,83 @@ __global__ void __launch_bounds__(256) vertexKernel(RenderArgs a) {
   a.vscr[o] = make_float2((c.x / c.w + 1.0f) * half_w - 0.5f, (c.y / c.w + 1.0f) * half_h - 0.5f);
 }
 
-// Raster pass: one CTA per (row band, hypothesis), z-buffer of packed
-// (depth, triangle) keys in shared memory; writes the band's triangle ids.
-__global__ void __launch_bounds__(kRenderThreads, 1) rasterKernel(RenderArgs a) {
+// Raster pass: one thread per (triangle, hypothesis). The coverage test and
+// depth key repeat the reference's per-pixel expressions over the reference's
+// bounding box (builtin_raster_renderer.cu:40-114), so the winning key of
+// every pixel -- the minimum over the same set of keys -- is the reference's.
+// The 64-bit atomicMin goes to the L2-resident z-buffer.
+__global__ void __launch_bounds__(kRasterThreads) rasterTriKernel(RenderArgs a) {
   tc::pdlTrigger();
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned long long* zbuf = reinterpret_cast<unsigned long long*>(smem_raw);
+  const int hyp = blockIdx.y;
+  const int tri = blockIdx.x * kRasterThreads + threadIdx.x;
+  const int nf = a.mesh.n_faces;
+  const int3 face = tri < nf ? loadFace(a, tri) : make_int3(0, 0, 0);  // the mesh is constant
+  tc::pdlWait();  // vertex positions and the cleared z-buffer are ready from here on
+  if (tri >= nf) return;
   const int width = a.p.input_width;
   const int height = a.p.input_height;
-  const int band = blockIdx.x;
-  const int hyp = blockIdx.y;
-  const int row0 = band * a.rows_per_band;  // rast rows (bottom-up)
-  const int row1 = min(height, row0 + a.rows_per_band);
-  const int band_rows = row1 - row0;
-  int* big_list = reinterpret_cast<int*>(smem_raw + static_cast<size_t>(a.rows_per_band) * width * 8);
-  __shared__ int big_count;
-  const int tid = threadIdx.x;
   const size_t vbase = static_cast<size_t>(hyp) * a.mesh.n_vertices;
-  const float4* vclip = a.vclip + vbase;
-  const float2* vscr = a.vscr + vbase;
-  if (tid == 0) big_count = 0;
-  for (int i = tid; i < band_rows * width; i += kRenderThreads) zbuf[i] = ~0ull;
-  __syncthreads();
-  tc::pdlWait();  // the vertex pass is complete from here on
-
+  const TriSetup s = setupTriangle(a.vclip + vbase, a.vscr + vbase, face, width, height);
+  if (s.min_x > s.max_x || s.min_y > s.max_y) return;
+  const int npx = (s.max_x - s.min_x + 1) * (s.max_y - s.min_y + 1);
+  if (npx > kSmallTriPixels) {
+    const int slot = atomicAdd(a.big_count, 1);
+    if (slot < a.big_cap) {
+      a.big_queue[slot] = make_int2(hyp, tri);
+      return;
+    }
+    // Queue full: this thread rasterizes the triangle itself (slower, same result).
+  }
+  // One flat loop over the bounding box (row terms refreshed on each new row):
+  // a warp runs as many iterations as its largest box.
   const float inv_w = 1.0f / static_cast<float>(width);
   const float inv_h = 1.0f / static_cast<float>(height);
-  const int nf = a.mesh.n_faces;
-  // The next triangle's indices are loaded one round ahead, so each round
-  // waits on one dependent load (the vertices) instead of two.
-  int3 next_face = tid < nf ? loadFace(a, tid) : make_int3(0, 0, 0);
-  for (int tri = tid; tri < nf; tri += kRenderThreads) {
-    const int3 face = next_face;
-    if (tri + kRenderThreads < nf) next_face = loadFace(a, tri + kRenderThreads);
-    const TriSetup s = setupTriangle(vclip, vscr, face, width, height);
-    const int y_lo = max(s.min_y, row0);
-    const int y_hi = min(s.max_y, row1 - 1);
-    if (s.min_x > s.max_x || y_lo > y_hi) {
-      continue;
-    }
-    if ((s.max_x - s.min_x + 1) * (y_hi - y_lo + 1) > kBigTriPixels) {
-      const int slot = atomicAdd(&big_count, 1);
-      if (slot < kBigListCap) {
-        big_list[slot] = tri;
-        continue;
-      }
-    }
-    // One flat loop over the bounding box (row terms refreshed on each new
-    // row): a warp runs as many iterations as its largest box, instead of
-    // its tallest box times its widest row.
-    const int npx = (s.max_x - s.min_x + 1) * (y_hi - y_lo + 1);
-    int px = s.min_x;
-    int py = y_lo;
-    float fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
-    float p0y = rowTerm(fy, s.p0);
-    float p1y = rowTerm(fy, s.p1);
-    float p2y = rowTerm(fy, s.p2);
-    unsigned long long* zrow = zbuf + (py - row0) * width;
-    for (int i = 0; i < npx; ++i) {
-      rasterPixel(s, px, inv_w, p0y, p1y, p2y, tri + 1, zrow);
-      if (++px > s.max_x) {
-        px = s.min_x;
-        ++py;
-        fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
-        p0y = rowTerm(fy, s.p0);
-        p1y = rowTerm(fy, s.p1);
-        p2y = rowTerm(fy, s.p2);
-        zrow += width;
-      }
+  int px = s.min_x;
+  int py = s.min_y;
+  float fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
+  float p0y = rowTerm(fy, s.p0);
+  float p1y = rowTerm(fy, s.p1);
+  float p2y = rowTerm(fy, s.p2);
+  unsigned long long* zrow = a.zbuf + (static_cast<size_t>(hyp) * height + py) * width;
+  for (int i = 0; i < npx; ++i) {
+    rasterPixel(s, px, inv_w, p0y, p1y, p2y, tri + 1, zrow);
+    if (++px > s.max_x) {
+      px = s.min_x;
+      ++py;
+      fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
+      p0y = rowTerm(fy, s.p0);
+      p1y = rowTerm(fy, s.p1);
+      p2y = rowTerm(fy, s.p2);
+      zrow += width;
     }
   }
-  __syncthreads();
-  // Large triangles: the whole CTA walks each one's pixels.
-  const int nbig = min(big_count, kBigListCap);
-  for (int b = 0; b < nbig; ++b) {
-    const int tri = big_list[b];
-    const TriSetup s = setupTriangle(a, vclip, vscr, tri, width, height);
-    const int y_lo = max(s.min_y, row0);
-    const int y_hi = min(s.max_y, row1 - 1);
+}
+
+// Large triangles: one warp per queued triangle, lanes over its pixels.
+__global__ void __launch_bounds__(kBigTriThreads) bigTriKernel(RenderArgs a) {
+  tc::pdlTrigger();
+  tc::pdlWait();  // the raster grid has queued every large triangle
+  const int count = min(*a.big_count, a.big_cap);
+  const int lane = threadIdx.x & 31;
+  const int nwarps = gridDim.x * (kBigTriThreads / 32);
+  const int width = a.p.input_width;
+  const int height = a.p.input_height;
+  const float inv_w = 1.0f / static_cast<float>(width);
+  const float inv_h = 1.0f / static_cast<float>(height);
+  for (int q = (blockIdx.x * kBigTriThreads + threadIdx.x) >> 5; q < count; q += nwarps) {
+    const int2 e = a.big_queue[q];
+    const size_t vbase = static_cast<size_t>(e.x) * a.mesh.n_vertices;
+    const TriSetup s = setupTriangle(a, a.vclip + vbase, a.vscr + vbase, e.y, width, height);
     const int bw = s.max_x - s.min_x + 1;
-    const int npx = bw * (y_hi - y_lo + 1);
-    for (int i = tid; i < npx; i += kRenderThreads) {
-      const int py = y_lo + i / bw;
+    const int npx = bw * (s.max_y - s.min_y + 1);
+    unsigned long long* z = a.zbuf + static_cast<size_t>(e.x) * height * width;
+    for (int i = lane; i < npx; i += 32) {
+      const int py = s.min_y + i / bw;
       const int px = s.min_x + i % bw;
       const float fy = (2.0f * py + 1.0f) * inv_h - 1.0f;
-      rasterPixel(s, px, inv_w, rowTerm(fy, s.p0), rowTerm(fy, s.p1), rowTerm(fy, s.p2), tri + 1,
-                  zbuf + (py - row0) * width);
+      rasterPixel(s, px, inv_w, rowTerm(fy, s.p0), rowTerm(fy, s.p1), rowTerm(fy, s.p2), e.y + 1,
+                  z + static_cast<size_t>(py) * width);
     }
-  }
-  __syncthreads();
-  // Resolve: triangle id per pixel (0 = background).
-  int32_t* ids = a.ids + (static_cast<size_t>(hyp) * height + row0) * width;
-  for (int i = tid; i < band_rows * width; i += kRenderThreads) {
-    const unsigned long long key = zbuf[i];
-    const int t = key == ~0ull ? 0 : static_cast<int>(key & 0xFFFFFFFFull);
-    ids[i] = t <= nf ? t : 0;
   }
 }
 
@@ -840,7 +838,10 @@ __global__ void __launch_bounds__(kShadeThreads) shadeKernel(RenderArgs a) {
   const size_t idx = static_cast<size_t>(hyp) * width * height + rem;
   const int py = rem / width;
   const int px = rem - py * width;
-  const int tri_plus_one = a.ids[idx];
+  // Resolve: the winning key's triangle (0 = background).
+  const unsigned long long key = a.zbuf[idx];
+  const int t = key == ~0ull ? 0 : static_cast<int>(key & 0xFFFFFFFFull);
+  const int tri_plus_one = t <= a.mesh.n_faces ? t : 0;
   float3 rgb = make_float3(0.0f, 0.0f, 0.0f);
   float3 xyz = make_float3(0.0f, 0.0f, 0.0f);
   if (tri_plus_one > 0) {
@@ -1050,70 +1051,39 @@ int validateParams(const fpk_params_t* p) {
   return 0;
 }
 
-size_t renderSmemBytes(int rows_per_band, int width) {
-  return static_cast<size_t>(rows_per_band) * width * 8 + kBigListCap * sizeof(int);
-}
-
-// Largest dynamic shared memory a render CTA may request on the current
-// device: the opt-in per-block limit minus the kernel's static shared memory.
-int maxDynamicSmem() {
+// SM count of the current device (cached per device).
+int renderSms() {
   static DeviceValue cache;
   return cache.get([](int dev) {
-    int optin = 0;
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncAttributes fa{};
-    const size_t stat = cudaFuncGetAttributes(&fa, rasterKernel) == cudaSuccess ? fa.sharedSizeBytes : 1024;
-    return optin - static_cast<int>(stat) - 256;
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
   });
 }
 
-// Rows per band: the whole crop when its z-buffer fits in shared memory; for
-// small batches the crop is split further so more SMs take part.
-int planBands(const fpk_params_t* p, int n, int* rows_per_band, int* bands) {
-  const int width = p->input_width;
-  const int height = p->input_height;
-  const int budget = maxDynamicSmem() - kBigListCap * static_cast<int>(sizeof(int));
-  int rows = budget / (width * 8);
-  if (rows <= 0) return fail("fpk: crop row does not fit in shared memory");
-  rows = rows < height ? rows : height;
-  int nb = (height + rows - 1) / rows;
-  const int want = n < 64 ? 8 : (n < 128 ? 2 : 1);
-  if (nb < want) {
-    nb = want < height ? want : height;
-    rows = (height + nb - 1) / nb;
-    nb = (height + rows - 1) / rows;
-  }
-  *rows_per_band = rows;
-  *bands = nb;
-  return 0;
-}
-
 // Workspace of one render call: clip positions (16 B) and pixel positions
-// (8 B) per (hypothesis, vertex), triangle ids (4 B) per crop pixel.
+// (8 B) per (hypothesis, vertex), the z-buffer (8 B per crop pixel) and the
+// large-triangle queue (8 B per entry; sized at a quarter of the
+// (hypothesis, vertex) count -- about an eighth of the triangles of a closed
+// mesh -- beyond which large triangles are rasterized by their own thread).
 struct RenderWorkspace {
-  size_t clip = 0, scr = 0, ids = 0, total = 0;
+  size_t clip = 0, scr = 0, zbuf = 0, count = 0, queue = 0, total = 0;
+  int cap = 0;
   RenderWorkspace(int n, int nv, int w, int h) {
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
     clip = up(static_cast<size_t>(n) * nv * 16);
     scr = up(static_cast<size_t>(n) * nv * 8);
-    ids = up(static_cast<size_t>(n) * w * h * 4);
-    total = clip + scr + ids;
+    zbuf = up(static_cast<size_t>(n) * w * h * 8);
+    count = 256;
+    const size_t c = std::min<size_t>(static_cast<size_t>(n) * nv / 4 + 4096, size_t{1} << 28);
+    cap = static_cast<int>(c);
+    queue = up(c * 8);
+    total = clip + scr + zbuf + count + queue;
   }
 };
 
 template <RenderOut kOut>
 int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  int rows = 0, nb = 0;
-  if (planBands(&a.p, a.n, &rows, &nb) != 0) return 1;
-  a.rows_per_band = rows;
-  const size_t smem = renderSmemBytes(rows, a.p.input_width);
-  static DeviceOnce smem_attr;
-  const cudaError_t ae = smem_attr.run(
-      [] { return cudaFuncSetAttribute(rasterKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxDynamicSmem()); });
-  if (ae != cudaSuccess) {
-    cudaGetLastError();
-    return fail(std::string("rasterKernel smem attribute: ") + cudaGetErrorString(ae));
-  }
   const RenderWorkspace ws(a.n, a.mesh.n_vertices, a.p.input_width, a.p.input_height);
   void* mem = workspace;
   if (mem == nullptr) {
@@ -1127,7 +1097,10 @@ int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStr
   unsigned char* base = static_cast<unsigned char*>(mem);
   a.vclip = reinterpret_cast<float4*>(base);
   a.vscr = reinterpret_cast<float2*>(base + ws.clip);
-  a.ids = reinterpret_cast<int32_t*>(base + ws.clip + ws.scr);
+  a.zbuf = reinterpret_cast<unsigned long long*>(base + ws.clip + ws.scr);
+  a.big_count = reinterpret_cast<int*>(base + ws.clip + ws.scr + ws.zbuf);
+  a.big_queue = reinterpret_cast<int2*>(base + ws.clip + ws.scr + ws.zbuf + ws.count);
+  a.big_cap = ws.cap;
   // Algorithmic bytes: mesh once, the frame once (rgb + depth) when packing,
   // and the outputs (NHWC fp32 rgb+xyz, or both packed network inputs).
   const double px = static_cast<double>(a.n) * a.p.input_width * a.p.input_height;
@@ -1137,12 +1110,14 @@ int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStr
                                                  : px * 12.0 * elt + a.img_w * static_cast<double>(a.img_h) * 7.0);
   int rc = 0;
   {
-    prof::countLaunch(prof::kRender);
-    prof::countLaunch(prof::kRender);
-    prof::countLaunch(prof::kRender);
+    for (int i = 0; i < 4; ++i) prof::countLaunch(prof::kRender);
     prof::Scope scope(prof::kRender, bytes, stream);
     cudaError_t e = launchPdl(vertexKernel, dim3((a.mesh.n_vertices + 255) / 256, a.n), dim3(256), 0, stream, a);
-    if (e == cudaSuccess) e = launchPdl(rasterKernel, dim3(nb, a.n), dim3(kRenderThreads), smem, stream, a);
+    if (e == cudaSuccess) {
+      e = launchPdl(rasterTriKernel, dim3((a.mesh.n_faces + kRasterThreads - 1) / kRasterThreads, a.n),
+                    dim3(kRasterThreads), 0, stream, a);
+    }
+    if (e == cudaSuccess) e = launchPdl(bigTriKernel, dim3(2 * renderSms()), dim3(kBigTriThreads), 0, stream, a);
     if (e == cudaSuccess) {
       e = launchPdl(shadeKernel<kOut>,
                     dim3((a.p.input_width * a.p.input_height + kShadeThreads - 1) / kShadeThreads, a.n),

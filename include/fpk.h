@@ -87,7 +87,8 @@ FP_API int fpk_crop_boxes(const float* poses, int n, fpk_intrinsics_t k, float d
 
 /* Device workspace (bytes, 256-byte aligned) of one fpk_render /
  * fpk_render_pack call over n hypotheses of a mesh with n_vertices vertices:
- * per (hypothesis, vertex) clip and pixel positions plus the triangle-id map.
+ * per (hypothesis, vertex) clip and pixel positions, the z-buffer of 64-bit
+ * (depth, triangle) keys per crop pixel and the queue of large triangles.
  * Passing workspace = NULL to those calls allocates it stream-ordered per call. */
 FP_API size_t fpk_render_workspace_bytes(int n, int n_vertices, const fpk_params_t* p);
 
@@ -96,8 +97,9 @@ FP_API size_t fpk_render_workspace_bytes(int n, int n_vertices, const fpk_params
  * (reference src/builtin_raster_renderer.cu:218-281, raster_kernels.cuh:336-495).
  * boxes are read (compute them with fpk_crop_boxes). tri_ids (optional,
  * [n*H*W] int32, rows bottom-up like the reference rast buffer) receives
- * triangle_index+1, 0 = background. Three launches: vertex transform,
- * shared-memory z-buffer raster, pixel-parallel shading. */
+ * triangle_index+1, 0 = background. Four launches: vertex transform,
+ * per-triangle raster into an L2-resident z-buffer, warp-per-triangle raster
+ * of large triangles, pixel-parallel resolve + shading. */
 FP_API int fpk_render(const fpk_mesh_t* mesh, const float* poses, const float* boxes, int n,
                       fpk_intrinsics_t k, const fpk_params_t* p, float* out_rgb, float* out_xyz,
                       int32_t* tri_ids, void* workspace, size_t workspace_bytes, void* stream);
@@ -112,8 +114,7 @@ FP_API int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, 
                     float* net_observed, void* stream);
 
 /* Crop boxes + rasterize + shade + crop-warp + pack (vertex transform,
- * shared-memory z-buffer raster per (hypothesis, row band), pixel-parallel
- * shading + packing), writing both
+ * per-triangle raster, pixel-parallel resolve + shading + packing), writing both
  * network inputs straight into the stem's space-to-depth KP8 layout: crop pixel
  * (y, x) of image i (rendered i = 0..n-1, observed n+i) goes to plane
  * ((y+3)%2)*2 + (x+3)%2, row i*gh*gw + ((y+3)/2)*gw + (x+3)/2 with
