@@ -115,6 +115,7 @@ struct Plan {
   uint32_t b_stage_bytes;
   uint32_t a_slot_bytes;  // CTA-pair kernel: window slot stride (1024-byte aligned)
   uint32_t a_plane_pitch;  // CTA-pair kernel: bytes between channel planes of a window (128-byte aligned)
+  int k_splits;            // single-CTA kernel: CTAs sharing one output tile's K range (1 = no split)
 };
 
 template <typename T>
@@ -208,6 +209,120 @@ __device__ __forceinline__ void storeRec8(unsigned char* base, long long plane_s
   }
 }
 
+// Where output row r lands in the layer's destination layout (see include/fpk.h).
+struct RowDst {
+  bool valid;
+  long long drow;
+  int ch_base;
+  int pos_row;
+};
+
+__device__ __forceinline__ RowDst rowDst(const fpk_gemm_desc_t& d, int r) {
+  RowDst o{r < d.rows, 0, 0, 0};
+  if (!o.valid) return o;
+  const int img = r / d.img_rows;
+  const int loc = r - img * d.img_rows;
+  const int gy = loc / d.grid_w;
+  const int gx = loc - gy * d.grid_w;
+  o.valid = gy < d.valid_h && gx < d.valid_w;
+  switch (d.dst_mode) {
+    case FPK_DST_S2D:
+      o.drow = static_cast<long long>(img) * d.dst_img_rows + ((gy + 1) >> 1) * d.dst_grid_w + ((gx + 1) >> 1);
+      o.ch_base = (((gy + 1) & 1) * 2 + ((gx + 1) & 1)) * d.cout;
+      break;
+    case FPK_DST_CONCAT:
+      o.drow = static_cast<long long>(img % d.img_mod) * d.img_rows + loc;
+      o.ch_base = (img / d.img_mod) * d.ch_step;
+      break;
+    case FPK_DST_TOKENS:
+      o.drow = static_cast<long long>(img) * d.valid_h * d.valid_w + gy * d.valid_w + gx;
+      o.pos_row = gy * d.valid_w + gx;
+      break;
+    default:
+      o.drow = r;
+  }
+  return o;
+}
+
+// Bias / residual / ReLU / positional embedding on the accumulator values of
+// output channels n..n+7 of one row, stored into the destination layout.
+template <typename T>
+__device__ __forceinline__ void finish8(const fpk_gemm_desc_t& d, const RowDst& rd, float* v, int n,
+                                        const uint4* res_rec, bool has_res) {
+  if (d.bias != nullptr) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(d.bias + n));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(d.bias + n + 4));
+    v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+    v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+  }
+  if (has_res) {
+    float rf[8];
+    unpackRec8<T>(res_rec, rf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] += rf[e];
+  }
+  if (d.relu) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = fmaxf(v[e], 0.0f);
+  }
+  if (d.dst_mode == FPK_DST_TOKENS && d.pos != nullptr) {
+    const float* pp = d.pos + static_cast<long long>(rd.pos_row) * d.cout + n;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
+  }
+  storeRec8<T>(static_cast<unsigned char*>(d.dst), d.dst_plane_stride, rd.ch_base + n, rd.drow, v);
+}
+
+// Split-K partial sums: split ks of output tile mn is a [BN/4][128][4] fp32
+// block (column quads outermost, rows, then the 4 columns of a quad), so a
+// warp's 32 consecutive rows read or write one contiguous 512-byte run.
+__device__ __forceinline__ float4* splitPartial(const fpk_gemm_desc_t& d, const Plan& pl, int bn, int mn,
+                                                int ks) {
+  return static_cast<float4*>(d.splitk_ws) + (static_cast<size_t>(mn) * pl.k_splits + ks) * (bn / 4) * kBlockM;
+}
+
+// Second launch of a split-K layer: one thread per (row, 8 output channels)
+// adds the k_splits partials in split order, then applies the layer's
+// epilogue (bias, residual, ReLU, positional embedding, destination layout).
+template <typename T>
+__global__ void __launch_bounds__(256) splitReduceKernel(const fpk_gemm_desc_t d, const Plan pl, int bn) {
+  pdlTrigger();
+  pdlWait();  // every split of the GEMM launch has written its partials
+  const int groups = bn / 8;
+  const long long i = static_cast<long long>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= static_cast<long long>(pl.m_tiles) * pl.n_tiles * groups * kBlockM) return;
+  const int row = static_cast<int>(i % kBlockM);
+  const long long t = i / kBlockM;
+  const int cg = static_cast<int>(t % groups);
+  const int mn = static_cast<int>(t / groups);
+  const int r = (mn / pl.n_tiles) * kBlockM + row;
+  const int n = (mn % pl.n_tiles) * bn + cg * 8;
+  const RowDst rd = rowDst(d, r);
+  if (!rd.valid) return;
+  const float4* p = splitPartial(d, pl, bn, mn, 0) + static_cast<size_t>(cg * 2) * kBlockM + row;
+  const size_t split_stride = static_cast<size_t>(bn / 4) * kBlockM;
+  float4 lo[8], hi[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    if (s < pl.k_splits) {
+      lo[s] = __ldcg(p + s * split_stride);
+      hi[s] = __ldcg(p + s * split_stride + kBlockM);
+    }
+  }
+  float v[8] = {lo[0].x, lo[0].y, lo[0].z, lo[0].w, hi[0].x, hi[0].y, hi[0].z, hi[0].w};
+#pragma unroll
+  for (int s = 1; s < 8; ++s) {
+    if (s < pl.k_splits) {
+      v[0] += lo[s].x; v[1] += lo[s].y; v[2] += lo[s].z; v[3] += lo[s].w;
+      v[4] += hi[s].x; v[5] += hi[s].y; v[6] += hi[s].z; v[7] += hi[s].w;
+    }
+  }
+  const bool has_res = d.residual != nullptr;
+  uint4 rr[2] = {};
+  if (has_res) loadRec8<T>(static_cast<const unsigned char*>(d.residual), d.res_plane_stride, n, r, rr);
+  finish8<T>(d, rd, v, n, rr, has_res);
+}
+
 // Epilogue of one accumulator row: converts TMEM columns [j0, j0 + kSpan) of
 // output row r (tile columns from n0) with bias / residual / ReLU / positional
 // embedding and stores them into the destination layout of the layer. t_base
@@ -215,36 +330,8 @@ __device__ __forceinline__ void storeRec8(unsigned char* base, long long plane_s
 template <typename T, int kSpan>
 __device__ __forceinline__ void epilogueRow(const fpk_gemm_desc_t& d, uint32_t t_base, int r, int n0, int j0) {
   const unsigned char* res = static_cast<const unsigned char*>(d.residual);
-  unsigned char* dst = static_cast<unsigned char*>(d.dst);
-  bool valid = r < d.rows;
-  long long drow = 0;
-  int ch_base = 0;
-  int pos_row = 0;
-  if (valid) {
-    const int img = r / d.img_rows;
-    const int loc = r - img * d.img_rows;
-    const int gy = loc / d.grid_w;
-    const int gx = loc - gy * d.grid_w;
-    valid = gy < d.valid_h && gx < d.valid_w;
-    switch (d.dst_mode) {
-      case FPK_DST_S2D:
-        drow = static_cast<long long>(img) * d.dst_img_rows + ((gy + 1) >> 1) * d.dst_grid_w +
-               ((gx + 1) >> 1);
-        ch_base = (((gy + 1) & 1) * 2 + ((gx + 1) & 1)) * d.cout;
-        break;
-      case FPK_DST_CONCAT:
-        drow = static_cast<long long>(img % d.img_mod) * d.img_rows + loc;
-        ch_base = (img / d.img_mod) * d.ch_step;
-        break;
-      case FPK_DST_TOKENS:
-        drow = static_cast<long long>(img) * d.valid_h * d.valid_w + gy * d.valid_w + gx;
-        pos_row = gy * d.valid_w + gx;
-        break;
-      default:
-        drow = r;
-    }
-  }
-  const bool has_res = valid && res != nullptr;
+  const RowDst rd = rowDst(d, r);
+  const bool has_res = rd.valid && res != nullptr;
   // Residual rows of the next 32 columns are fetched while the current
   // 32 are converted and stored.
   uint4 rv[4][2] = {}, rn[4][2] = {};
@@ -261,35 +348,13 @@ __device__ __forceinline__ void epilogueRow(const fpk_gemm_desc_t& d, uint32_t t
       for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j + 32 + g * 8, r, rn[g]);
     }
     tmemWaitLd();
-    if (valid) {
+    if (rd.valid) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const int n = n0 + j + g * 8;
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[g * 8 + e]);
-        if (d.bias != nullptr) {
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(d.bias + n));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(d.bias + n + 4));
-          v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
-          v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
-        }
-        if (has_res) {
-          float rf[8];
-          unpackRec8<T>(rv[g], rf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] += rf[e];
-        }
-        if (d.relu) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = fmaxf(v[e], 0.0f);
-        }
-        if (d.dst_mode == FPK_DST_TOKENS && d.pos != nullptr) {
-          const float* pp = d.pos + static_cast<long long>(pos_row) * d.cout + n;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
-        }
-        storeRec8<T>(dst, d.dst_plane_stride, ch_base + n, drow, v);
+        finish8<T>(d, rd, v, n0 + j + g * 8, rv[g], has_res);
       }
     }
 #pragma unroll
@@ -367,8 +432,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tcFenceAfter();
   pdlWait();  // the previous layer's output (this layer's input) is complete from here on
   const uint32_t tmem = sm->tmem_base;
-  const int n_tiles_total = pl.m_tiles * pl.n_tiles;
+  // Work items: output tiles, each split into k_splits contiguous chunk ranges.
+  const int n_tiles_total = pl.m_tiles * pl.n_tiles * pl.k_splits;
   const int taps_cw = d.taps * pl.cw;
+  auto chunkRange = [&](int tile, int* c0, int* c1) {
+    const int ks = tile % pl.k_splits;
+    *c0 = ks * pl.n_chunks / pl.k_splits;
+    *c1 = (ks + 1) * pl.n_chunks / pl.k_splits;
+  };
 
   if (warp == 0) {
     {
@@ -382,9 +453,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t a_phase = 0, b_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
-        const int m0 = (tile / pl.n_tiles) * kTileM;
-        const int n0 = (tile % pl.n_tiles) * BN;
-        for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
+        const int mn = tile / pl.k_splits;
+        const int m0 = (mn / pl.n_tiles) * kTileM;
+        const int n0 = (mn % pl.n_tiles) * BN;
+        int c0, c1;
+        chunkRange(tile, &c0, &c1);
+        for (int ch = c0; ch < c1 && ok; ++ch) {
           ok = warpWaitBar(&sm->a_empty[slot], a_phase ^ 1, err, 11);
           if (!ok) break;
           if (lane == 0) mbarExpectTx(&sm->a_full[slot], pl.a_win_bytes);
@@ -445,7 +519,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tcFenceAfter();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * MH * BN);
         uint32_t accumulate = 0;
-        for (int ch = 0; ch < pl.n_chunks && ok; ++ch) {
+        int c0, c1;
+        chunkRange(tile, &c0, &c1);
+        for (int ch = c0; ch < c1 && ok; ++ch) {
           ok = warpWaitBar(&sm->a_full[slot], a_phase, err, 14);
           if (!ok) break;
           tcFenceAfter();
@@ -488,15 +564,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = m_half * kBlockM + quarter * 32 + lane;
     uint32_t t_iter = 0;
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++t_iter) {
-      const int m0 = (tile / pl.n_tiles) * kTileM;
-      const int n0 = (tile % pl.n_tiles) * BN;
+      const int mn = tile / pl.k_splits;
+      const int m0 = (mn / pl.n_tiles) * kTileM;
+      const int n0 = (mn % pl.n_tiles) * BN;
       const int buf = static_cast<int>(t_iter % kBufs);
       if (!waitBar(&sm->acc_full[buf], (t_iter / kBufs) & 1, err, 17)) break;
       tcFenceAfter();
       const uint32_t t_base =
           tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
           static_cast<uint32_t>((buf * MH + m_half) * BN);
-      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, MH == 1 ? pair * kSpan : 0);
+      const int j0 = MH == 1 ? pair * kSpan : 0;
+      if (MH == 1 && pl.k_splits > 1) {
+        // Split K: this warp's 32 rows x kSpan columns of the partial sum go
+        // to the scratch; the reduce launch adds the splits and stores.
+        float4* own = splitPartial(d, pl, BN, mn, tile % pl.k_splits) + row_in_tile;
+#pragma unroll 1
+        for (int j = j0; j < j0 + kSpan; j += 32) {
+          uint32_t acc[32];
+          FPB_TMEM_LD32(t_base + j, acc);
+          tmemWaitLd();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            __stcg(own + static_cast<size_t>((j >> 2) + q) * kBlockM,
+                   make_float4(__uint_as_float(acc[4 * q]), __uint_as_float(acc[4 * q + 1]),
+                               __uint_as_float(acc[4 * q + 2]), __uint_as_float(acc[4 * q + 3])));
+          }
+        }
+        tcFenceBefore();
+        __syncwarp();
+        if (lane == 0) mbarArrive(&sm->acc_empty[buf]);
+        continue;
+      }
+      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, j0);
       tcFenceBefore();
       __syncwarp();
       if (lane == 0) mbarArrive(&sm->acc_empty[buf]);
@@ -849,10 +948,16 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
     cudaGetLastError();
     return fail(std::string("fpk_gemm smem attribute: ") + cudaGetErrorString(ae));
   }
-  const int tiles = pl.m_tiles * pl.n_tiles;
+  const int tiles = pl.m_tiles * pl.n_tiles * pl.k_splits;
   const int grid = tiles < numSms() ? tiles : numSms();
   prof::countLaunch(prof::kGemm);
-  const cudaError_t e = launchPdl(gemmKernel<T, BN, MH>, dim3(grid), dim3(kThreads), smem, stream, d, pl, map);
+  cudaError_t e = launchPdl(gemmKernel<T, BN, MH>, dim3(grid), dim3(kThreads), smem, stream, d, pl, map);
+  if (e == cudaSuccess && pl.k_splits > 1) {
+    prof::countLaunch(prof::kGemm);
+    const long long threads = static_cast<long long>(pl.m_tiles) * pl.n_tiles * (BN / 8) * kBlockM;
+    e = launchPdl(splitReduceKernel<T>, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0, stream, d,
+                  pl, BN);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(std::string("gemmKernel launch: ") + cudaGetErrorString(e));
@@ -987,6 +1092,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     return fail("fpk_gemm: pointers and plane strides must be 16-byte aligned");
   }
   Plan pl{};
+  pl.k_splits = 1;
   pl.cw = d.cin < stage_elems ? d.cin : stage_elems;
   pl.planes = pl.cw * esize / 16;
   pl.n_chunks = d.cin / pl.cw;
@@ -1109,6 +1215,18 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     mh = 2;
   } else if (!plan(1)) {
     return fail("fpk_gemm: activation window too large for shared memory");
+  }
+  // Split K when the output tiles fill less than half of the GPU (small
+  // batches, e.g. tracking one hypothesis) and the caller gave scratch: up to
+  // 8 chunk ranges per tile (the reduce kernel adds at most 8 partials), at
+  // most one CTA per SM in all.
+  if (mh == 1 && d.splitk_ws != nullptr && pl.n_chunks >= 2) {
+    const int tiles = pl.m_tiles * pl.n_tiles;
+    int ks = tiles * 2 <= numSms() ? numSms() / tiles : 1;
+    ks = ks < pl.n_chunks ? ks : pl.n_chunks;
+    ks = ks < kEpilogueWarps ? ks : kEpilogueWarps;
+    while (ks > 1 && static_cast<long long>(tiles) * ks * bn * kBlockM * 4 > d.splitk_ws_bytes) --ks;
+    if (ks > 1 && reinterpret_cast<uintptr_t>(d.splitk_ws) % 16 == 0) pl.k_splits = ks;
   }
   const size_t smem = 1024 + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes +
                       static_cast<size_t>(pl.a_slots) * pl.a_win_bytes + sizeof(Smem);

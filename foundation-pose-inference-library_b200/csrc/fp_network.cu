@@ -389,12 +389,17 @@ NetworkRunner::NetworkRunner(const std::string& refine_path, const std::string& 
     allocations_.push_back(e);
     check(cudaMemset(e, 0, 16), "zero error flag");
     err_ = static_cast<int*>(e);
+    splitk_bytes_ = 24ll << 20;
+    check(cudaMalloc(&splitk_, static_cast<size_t>(splitk_bytes_)), "cudaMalloc split-K scratch");
+    allocations_.push_back(splitk_);
   } catch (...) {
     for (void* p : allocations_) cudaFree(p);
     allocations_.clear();
     throw;
   }
 }
+
+void NetworkRunner::clearError(cudaStream_t s) { check(cudaMemsetAsync(err_, 0, sizeof(int), s), "reset error flag"); }
 
 NetworkRunner::~NetworkRunner() {
   for (void* p : allocations_) cudaFree(p);
@@ -445,6 +450,8 @@ void NetworkRunner::gemm(const ConvLayer& L, const Planar& a, long long a_row0, 
   d.pos = pos;
   d.dtype = dtype();
   d.error_flag = err_;
+  d.splitk_ws = split_k_ ? splitk_ : nullptr;
+  d.splitk_ws_bytes = split_k_ ? splitk_bytes_ : 0;
   const double valid_rows = static_cast<double>(rows / img_rows) * valid_h * valid_w;
   prof::Scope scope(prof::kGemm, valid_rows * L.flops_per_row, s);
   if (fpk_gemm(&d, s) != 0) throw std::runtime_error(fpk_last_error());
@@ -483,6 +490,7 @@ void NetworkRunner::encoder(const Network& net, int n, long long stem_row0, cuda
 
 void NetworkRunner::refine(int count, int first_chunk, float* delta_t, float* delta_r, cudaStream_t s) {
   if (count <= 0 || count > max_batch_) throw std::runtime_error("refine batch exceeds the prepared maximum");
+  split_k_ = count == 1;
   Act& a = *act_;
   const Network& net = *refine_;
   const int dt = dtype();
@@ -534,6 +542,7 @@ void NetworkRunner::score(int n, float* scores, cudaStream_t s) {
 
 void NetworkRunner::scoreFeatures(int n, float* features, cudaStream_t s) {
   if (n <= 0 || n > max_batch_) throw std::runtime_error("score batch exceeds the prepared maximum");
+  split_k_ = n == 1;
   Act& a = *act_;
   const Network& net = *score_;
   const int dt = dtype();

@@ -85,6 +85,8 @@ class NetworkRunner {
   void loadNchw(const float* rendered, const float* observed, int n, cudaStream_t s);
   // Device error flag of the pipelined kernels (0 = ok).
   int* errorFlag() const { return err_; }
+  // After a pipeline timeout has been reported: zero the error flag.
+  void clearError(cudaStream_t s);
   // Algorithmic FLOPs of one forward per hypothesis (for rooflines).
   double refineFlopsPerHyp() const;
   double scoreFlopsPerHyp() const;
@@ -106,6 +108,13 @@ class NetworkRunner {
   Planar stem_;
   std::unique_ptr<Act> act_;
   int* err_ = nullptr;
+  // Split-K scratch for one-hypothesis passes (track): layers of a single
+  // image pair fill a few SMs per tile row, so their K range is split across
+  // CTAs (see fpk_gemm_desc_t). Batched passes never split, which keeps every
+  // hypothesis's result independent of the batch it runs in.
+  void* splitk_ = nullptr;
+  long long splitk_bytes_ = 0;
+  bool split_k_ = false;
 };
 
 }  // namespace fpb

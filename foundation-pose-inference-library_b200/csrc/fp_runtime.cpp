@@ -507,7 +507,7 @@ struct FoundationPose::Impl {
     checkCuda(cudaMemcpyAsync(&host, flag, sizeof(int), cudaMemcpyDeviceToHost, s()), "read error flag");
     stream->synchronize();
     if (host != 0) {
-      checkCuda(cudaMemsetAsync(flag, 0, sizeof(int), s()), "reset error flag");
+      BuiltinInferenceRunner::run([&] { builtin_runner->net().clearError(s()); });
       stream->synchronize();
       throw FoundationPoseError("network kernel pipeline timed out (code " + std::to_string(host) + ")");
     }

@@ -170,7 +170,7 @@ class GemmDesc(C.Structure):
         ("dst_mode", C.c_int), ("img_rows", C.c_int), ("grid_w", C.c_int), ("valid_h", C.c_int),
         ("valid_w", C.c_int), ("dst_img_rows", C.c_int), ("dst_grid_w", C.c_int),
         ("img_mod", C.c_int), ("ch_step", C.c_int), ("pos", C.c_void_p), ("dtype", C.c_int),
-        ("error_flag", C.c_void_p),
+        ("error_flag", C.c_void_p), ("splitk_ws", C.c_void_p), ("splitk_ws_bytes", C.c_longlong),
     ]
 
 

@@ -205,6 +205,14 @@ typedef struct fpk_gemm_desc {
   const float* pos;
   int dtype;       /* FPK_DTYPE_F16, FPK_DTYPE_BF16 or FPK_DTYPE_F32 (TF32 math) */
   int* error_flag; /* device int32; set non-zero if a pipeline wait times out */
+  /* Optional split-K scratch (device, or NULL). When given, a layer whose
+   * output tiles fill less than half of the GPU splits its K range over up to
+   * 8 CTAs per tile, which write fp32 partial sums here; a second launch adds
+   * the partials of each output in split order and applies the epilogue, so
+   * results are deterministic for a given layer and row count (they differ
+   * from the unsplit sum in the last bits). Nothing in it needs initialising. */
+  void* splitk_ws;
+  long long splitk_ws_bytes;
 } fpk_gemm_desc_t;
 
 FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);

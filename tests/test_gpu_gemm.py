@@ -308,3 +308,74 @@ def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout, cin):
         assert err.item() == 0
         outs.append(out.get())
     assert torch.equal(outs[0], outs[1])
+
+
+# Split K (tracking one hypothesis): few output tiles, so each tile's K range
+# is split over several CTAs whose fp32 partial sums a second launch adds in
+# split order. Checked against torch, against the unsplit kernel, and for
+# run-to-run bit identity.
+@pytest.mark.parametrize("cin,cout,hw,dtype", [(256, 256, 40, FPK_DTYPE_F16), (512, 512, 20, FPK_DTYPE_BF16),
+                                               (128, 128, 40, FPK_DTYPE_F16), (256, 256, 40, FPK_DTYPE_F32)])
+def test_split_k_conv3x3(fpk, err, cin, cout, hw, dtype):
+    g = torch.Generator().manual_seed(cin + hw)
+    dt = DT[dtype]
+    H = W = hw
+    gw = W + 1
+    img_rows = (H + 1) * gw
+    X = torch.randn(1, cin, H, W, generator=g)
+    R = torch.randn(1, cout, H, W, generator=g)
+    Wt = torch.randn(cout, cin, 3, 3, generator=g) / math.sqrt(9 * cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+
+    def to_grid(t):
+        z = torch.zeros(1, H + 1, W + 1, t.shape[1])
+        z[:, :H, :W] = t.permute(0, 2, 3, 1)
+        return z.reshape(img_rows, t.shape[1])
+
+    pa = Planar(img_rows, cin, dt).set(to_grid(X).to(DEV))
+    pr = Planar(img_rows, cout, dt).set(to_grid(R).to(DEV))
+    taps = [(ky - 1) * gw + (kx - 1) for ky in range(3) for kx in range(3)]
+    w = chunk_major(Wt.permute(0, 2, 3, 1).reshape(cout, 9, cin), dtype).to(dt).to(DEV)
+    ws = torch.zeros(24 << 20, dtype=torch.uint8, device=DEV)
+    outs = []
+    for split in (False, True, True):
+        out = Planar(img_rows, cout, dt)
+        d = make_desc(pa, img_rows, cin, taps, w, cout, out, dtype, err, bias=b, residual=pr, relu=True,
+                      img_rows=img_rows, grid_w=gw, valid_h=H, valid_w=W)
+        if split:
+            d.splitk_ws, d.splitk_ws_bytes = ws.data_ptr(), ws.numel()
+        gemm(fpk, d)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        outs.append(out.get().reshape(H + 1, W + 1, cout))
+    assert torch.count_nonzero(ws) > 0, "the split path did not run"
+    assert torch.equal(outs[1], outs[2]), "split-K results must be identical run to run"
+    ref = F.conv2d(X.to(dt).float().to(DEV), Wt.to(dt).float().to(DEV), b, padding=1)
+    ref = torch.relu(ref + R.to(dt).float().to(DEV))[0].permute(1, 2, 0)
+    close(outs[1][:H, :W], ref)
+    close(outs[1], outs[0])
+    assert torch.count_nonzero(outs[1][H]) == 0 and torch.count_nonzero(outs[1][:, W]) == 0
+
+
+def test_split_k_tokens_linear(fpk, err):
+    """The 400-token linears of one hypothesis (TOKENS destination with the
+    positional embedding) through the split path."""
+    g = torch.Generator().manual_seed(3)
+    dt = torch.float16
+    m, cin, cout = 400, 512, 1536
+    A = torch.randn(m, cin, generator=g)
+    Wm = torch.randn(cout, cin, generator=g) / math.sqrt(cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+    pos = (torch.randn(m, cout, generator=g) * 0.1).to(DEV)
+    pa = Planar(m, cin, dt).set(A.to(DEV))
+    out = Planar(m, cout, dt)
+    w = chunk_major(Wm.reshape(cout, 1, cin), FPK_DTYPE_F16).to(dt).to(DEV)
+    ws = torch.zeros(24 << 20, dtype=torch.uint8, device=DEV)
+    d = make_desc(pa, m, cin, [0], w, cout, out, FPK_DTYPE_F16, err, bias=b, mode=FPK_DST_TOKENS,
+                  img_rows=m, grid_w=20, valid_h=20, valid_w=20, pos=pos)
+    d.splitk_ws, d.splitk_ws_bytes = ws.data_ptr(), ws.numel()
+    gemm(fpk, d)
+    torch.cuda.synchronize()
+    assert err.item() == 0 and torch.count_nonzero(ws) > 0
+    ref = A.to(dt).float().to(DEV) @ Wm.to(dt).float().to(DEV).T + b + pos
+    close(out.get(), ref)
