@@ -68,6 +68,13 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    # Programs linked against the library record its soname (SOVERSION 1, as
+    # the reference's CMake build sets it); the loader resolves that name.
+    soname = LIB.with_name(LIB.name + ".1")
+    if not soname.is_symlink() or os.readlink(soname) != LIB.name:
+        if soname.exists() or soname.is_symlink():
+            soname.unlink()
+        soname.symlink_to(LIB.name)
     return LIB
 
 

@@ -444,80 +444,6 @@ std::vector<Mat3f> makeRotationGrid(const Config& config) {
   return out;
 }
 
-// Model-free mesh: back-project every `stride`-th masked, valid depth pixel of
-// each reference view into the world frame (camera_to_world), then triangulate
-// neighbouring grid samples whose depths differ by at most the edge threshold.
-Mesh reconstructReferenceMesh(std::span<const ModelFreeReferenceView> refs, const Config& config) {
-  if (static_cast<int>(refs.size()) < config.model_free_min_reference_images) {
-    throw FoundationPoseError("Model-free mode requires at least one reference image");
-  }
-  std::size_t total = 0;
-  for (const auto& r : refs) {
-    if (r.intrinsics.fx <= 0.0f || r.intrinsics.fy <= 0.0f) {
-      throw FoundationPoseError("Camera intrinsics must have positive focal lengths");
-    }
-    if (r.width <= 0 || r.height <= 0 || !r.rgb_u8 || !r.depth_m || !r.mask_u8) {
-      throw FoundationPoseError("Each model-free reference needs RGB, depth, mask, and dimensions");
-    }
-    total += static_cast<std::size_t>(r.width) * r.height;
-  }
-  const int max_v = std::max(config.model_free_max_vertices, 4);
-  const int adaptive = std::max(1, static_cast<int>(std::ceil(std::sqrt(static_cast<double>(total) / max_v))));
-  const int stride = std::max(config.model_free_sample_stride, adaptive);
-  auto valid = [&](float z) { return std::isfinite(z) && z >= config.depth_min && z < config.depth_max; };
-  auto smooth = [&](float a, float b, float c) {
-    const float t = config.model_free_depth_edge_threshold;
-    return std::abs(a - b) <= t && std::abs(a - c) <= t && std::abs(b - c) <= t;
-  };
-  Mesh mesh;
-  mesh.source_path = "model_free_references";
-  for (const auto& r : refs) {
-    const std::size_t px = static_cast<std::size_t>(r.width) * r.height;
-    std::vector<int> grid(px, -1);
-    std::vector<float> zs(px, 0.0f);
-    for (int y = 0; y < r.height; y += stride) {
-      for (int x = 0; x < r.width; x += stride) {
-        const std::size_t i = static_cast<std::size_t>(y) * r.width + x;
-        const float z = r.depth_m[i];
-        if (r.mask_u8[i] == 0 || !valid(z)) continue;
-        if (mesh.vertices.size() >= static_cast<std::size_t>(max_v)) break;
-        const Vec3f cam{(static_cast<float>(x) - r.intrinsics.cx) * z / r.intrinsics.fx,
-                        (static_cast<float>(y) - r.intrinsics.cy) * z / r.intrinsics.fy, z};
-        const Mat4f& m = r.camera_to_world;
-        mesh.vertices.push_back({m(0, 0) * cam.x + m(0, 1) * cam.y + m(0, 2) * cam.z + m(0, 3),
-                                 m(1, 0) * cam.x + m(1, 1) * cam.y + m(1, 2) * cam.z + m(1, 3),
-                                 m(2, 0) * cam.x + m(2, 1) * cam.y + m(2, 2) * cam.z + m(2, 3)});
-        mesh.vertex_colors.push_back({r.rgb_u8[3 * i], r.rgb_u8[3 * i + 1], r.rgb_u8[3 * i + 2]});
-        grid[i] = static_cast<int>(mesh.vertices.size() - 1);
-        zs[i] = z;
-      }
-      if (mesh.vertices.size() >= static_cast<std::size_t>(max_v)) break;
-    }
-    for (int y = 0; y + stride < r.height; y += stride) {
-      for (int x = 0; x + stride < r.width; x += stride) {
-        const std::size_t ia = static_cast<std::size_t>(y) * r.width + x;
-        const std::size_t ib = ia + stride;
-        const std::size_t ic = ia + static_cast<std::size_t>(stride) * r.width;
-        const std::size_t id = ic + stride;
-        const int a = grid[ia], b = grid[ib], c = grid[ic], d = grid[id];
-        if (a >= 0 && b >= 0 && c >= 0 && smooth(zs[ia], zs[ib], zs[ic])) {
-          mesh.faces.push_back({static_cast<std::uint32_t>(a), static_cast<std::uint32_t>(b),
-                                static_cast<std::uint32_t>(c)});
-        }
-        if (b >= 0 && d >= 0 && c >= 0 && smooth(zs[ib], zs[id], zs[ic])) {
-          mesh.faces.push_back({static_cast<std::uint32_t>(b), static_cast<std::uint32_t>(d),
-                                static_cast<std::uint32_t>(c)});
-        }
-      }
-    }
-  }
-  if (mesh.vertices.size() < 4 || mesh.faces.empty()) {
-    throw FoundationPoseError("Model-free reconstruction produced too little geometry; check masks and depth");
-  }
-  computeVertexNormals(mesh);
-  return mesh;
-}
-
 }  // namespace fpb_host
 }  // namespace foundation_pose_nvidia
 

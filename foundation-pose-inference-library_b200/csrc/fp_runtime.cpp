@@ -12,24 +12,33 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <exception>
 #include <format>
 #include <functional>
+#include <latch>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <string_view>
 #include <thread>
 #include <utility>
 #include <vector>
 
+#include "foundation_pose_nvidia/builtin_raster_renderer.hpp"
 #include "foundation_pose_nvidia/c_api.h"
 #include "foundation_pose_nvidia/foundation_pose.hpp"
+#include "foundation_pose_nvidia/tensorrt_runner.hpp"
 #include "fp_host.hpp"
 #include "fp_network.hpp"
 #include "fpk.h"
+
+namespace fpb {
+int fail(const std::string& msg);
+}
 
 namespace foundation_pose_nvidia {
 
@@ -177,36 +186,49 @@ void uploadMesh(const Mesh& mesh, DeviceMesh& dst, cudaStream_t s) {
   checkCuda(cudaStreamSynchronize(s), "upload mesh");
 }
 
-// Built-in renderer behind the IRenderer seam (fpk_render).
-class BuiltinRenderer final : public IRenderer {
- public:
-  explicit BuiltinRenderer(const Config& c) : params_(toParams(c)), max_batch_(std::max(1, c.n_hypotheses)) {}
-  void reserveForMesh(int num_vertices, int) override {
-    const std::size_t bytes = fpk_render_workspace_bytes(max_batch_, num_vertices, &params_);
-    if (bytes > workspace_.bytes()) workspace_.allocate(bytes);
-  }
-  void render(const DeviceMesh& mesh, const float* poses, const float* crop_boxes, int batch_size,
-              CameraIntrinsics k, int, int, float3* out_rgb, float3* out_xyz,
-              cudaStream_t stream) override {
-    if (mesh.num_vertices <= 0 || mesh.num_faces <= 0) {
-      throw FoundationPoseError("builtin renderer received an empty mesh");
-    }
-    const std::size_t need = fpk_render_workspace_bytes(batch_size, mesh.num_vertices, &params_);
-    if (need > workspace_.bytes()) {
-      checkCuda(cudaStreamSynchronize(stream), "renderer workspace resize");
-      workspace_.allocate(need);
-    }
-    const fpk_mesh_t m = meshView(mesh);
-    fpkCheck(fpk_render(&m, poses, crop_boxes, batch_size, toK(k), &params_,
-                        reinterpret_cast<float*>(out_rgb), reinterpret_cast<float*>(out_xyz), nullptr,
-                        workspace_.data(), workspace_.bytes(), stream));
-  }
+}  // namespace
 
- private:
-  fpk_params_t params_;
-  int max_batch_;
-  DeviceBuffer workspace_;
+// Built-in renderer behind the IRenderer seam (fpk_render into the caller's
+// NHWC buffers; the estimator fuses it with the pack when it also runs the
+// built-in networks).
+struct BuiltinRasterRenderer::Impl {
+  fpk_params_t params;
+  int max_batch;
+  DeviceBuffer workspace;
 };
+
+BuiltinRasterRenderer::BuiltinRasterRenderer(const Config& config, int device_id, int max_batch)
+    : impl_(std::make_unique<Impl>(Impl{toParams(config), std::max(1, max_batch), DeviceBuffer{}})) {
+  int current = -1;
+  checkCuda(cudaGetDevice(&current), "cudaGetDevice");
+  if (current != device_id) checkCuda(cudaSetDevice(device_id), "cudaSetDevice");
+}
+
+BuiltinRasterRenderer::~BuiltinRasterRenderer() = default;
+
+void BuiltinRasterRenderer::reserveForMesh(int num_vertices, int) {
+  const std::size_t bytes = fpk_render_workspace_bytes(impl_->max_batch, num_vertices, &impl_->params);
+  if (bytes > impl_->workspace.bytes()) impl_->workspace.allocate(bytes);
+}
+
+void BuiltinRasterRenderer::render(const DeviceMesh& mesh, const float* poses, const float* crop_boxes,
+                                   int batch_size, CameraIntrinsics k, int, int, float3* out_rgb, float3* out_xyz,
+                                   cudaStream_t stream) {
+  if (mesh.num_vertices <= 0 || mesh.num_faces <= 0) {
+    throw FoundationPoseError("builtin renderer received an empty mesh");
+  }
+  const std::size_t need = fpk_render_workspace_bytes(batch_size, mesh.num_vertices, &impl_->params);
+  if (need > impl_->workspace.bytes()) {
+    checkCuda(cudaStreamSynchronize(stream), "renderer workspace resize");
+    impl_->workspace.allocate(need);
+  }
+  const fpk_mesh_t m = meshView(mesh);
+  fpkCheck(fpk_render(&m, poses, crop_boxes, batch_size, toK(k), &impl_->params, reinterpret_cast<float*>(out_rgb),
+                      reinterpret_cast<float*>(out_xyz), nullptr, impl_->workspace.data(), impl_->workspace.bytes(),
+                      stream));
+}
+
+namespace {
 
 // Default-renderer selection (reference src/foundation_pose.cpp:40-68): the
 // built-in rasterizer unless FP_RENDERER=nvdiffrast, which loads the renderer
@@ -250,7 +272,7 @@ const RendererPlugin& rendererPlugin() {
 std::unique_ptr<IRenderer> makeDefaultRenderer(const Config& config, int device_id, int max_batch) {
   const char* choice = std::getenv("FP_RENDERER");
   if (choice == nullptr || std::string_view(choice) != "nvdiffrast") {
-    return std::make_unique<BuiltinRenderer>(config);
+    return std::make_unique<BuiltinRasterRenderer>(config, device_id, max_batch);
   }
   const RendererPlugin& plugin = rendererPlugin();
   if (plugin.handle == nullptr) {
@@ -282,82 +304,84 @@ fpb::NetPrecision toNetPrecision(TensorrtPrecision p) {
 
 }  // namespace
 
+// Exceptions of the network code surface as FoundationPoseError.
+template <class F>
+void runNet(F&& f) {
+  try {
+    f();
+  } catch (const FoundationPoseError&) {
+    throw;
+  } catch (const std::exception& e) {
+    throw FoundationPoseError(e.what());
+  }
+}
+
 // Built-in RefineNet/ScoreNet behind the IInferenceRunner seam. The networks
 // are created on first use (like the reference's lazily built engines).
-class BuiltinInferenceRunner final : public IInferenceRunner {
- public:
-  BuiltinInferenceRunner(RuntimeOptions o, Config c, int max_batch)
-      : opts_(std::move(o)), cfg_(c), max_batch_(max_batch) {
-    const int bs = c.batch_size > 0 ? c.batch_size : max_batch;
-    engine_batch_ = std::min(max_batch, bs);
-    if (engine_batch_ <= 0 || max_batch % engine_batch_ != 0) {
-      throw FoundationPoseError("max_batch (" + std::to_string(max_batch) +
-                                ") must be divisible by effective_bs (" + std::to_string(engine_batch_) + ")");
-    }
-  }
+struct TensorRtRunner::Impl {
+  RuntimeOptions opts;
+  Config cfg;
+  int max_batch = 0;
+  int engine_batch = 0;
+  std::unique_ptr<fpb::NetworkRunner> net_;
 
   fpb::NetworkRunner& net() {
     if (!net_) {
-      if (opts_.refine_model_path.empty()) throw FoundationPoseError("refine_model_path is required");
-      if (opts_.score_model_path.empty()) throw FoundationPoseError("score_model_path is required");
-      try {
-        net_ = std::make_unique<fpb::NetworkRunner>(opts_.refine_model_path, opts_.score_model_path,
-                                                     toNetPrecision(cfg_.tensorrt_precision), max_batch_,
-                                                     cfg_.input_width, cfg_.input_height);
-      } catch (const FoundationPoseError&) {
-        throw;
-      } catch (const std::exception& e) {
-        throw FoundationPoseError(e.what());
-      }
+      if (opts.refine_model_path.empty()) throw FoundationPoseError("refine_model_path is required");
+      if (opts.score_model_path.empty()) throw FoundationPoseError("score_model_path is required");
+      runNet([&] {
+        net_ = std::make_unique<fpb::NetworkRunner>(opts.refine_model_path, opts.score_model_path,
+                                                    toNetPrecision(cfg.tensorrt_precision), max_batch,
+                                                    cfg.input_width, cfg.input_height);
+      });
     }
     return *net_;
   }
-
-  void prepareForBatch(int batch_size) override {
-    if (batch_size <= 0 || batch_size > max_batch_) {
-      throw FoundationPoseError("prepare batch size exceeds configured maximum");
-    }
-    (void)net();
-  }
-
-  void enqueueRefine(const float* rendered, const float* observed, float* dt, float* dr, int batch,
-                     cudaStream_t stream) override {
-    if (batch <= 0 || batch > max_batch_) throw FoundationPoseError("refine batch size exceeds configured maximum");
-    const std::size_t stride = static_cast<std::size_t>(6) * cfg_.input_width * cfg_.input_height;
-    for (int off = 0; off < batch; off += engine_batch_) {
-      const int chunk = std::min(engine_batch_, batch - off);
-      net().loadNchw(rendered + off * stride, observed + off * stride, chunk, stream);
-      run([&] { net().refine(chunk, 0, dt + 3 * off, dr + 3 * off, stream); });
-    }
-  }
-
-  void enqueueScore(const float* rendered, const float* observed, float* scores, int batch,
-                    cudaStream_t stream) override {
-    if (batch <= 0 || batch > max_batch_) throw FoundationPoseError("score batch size exceeds configured maximum");
-    net().loadNchw(rendered, observed, batch, stream);
-    run([&] { net().score(batch, scores, stream); });
-  }
-
-  int engineBatch() const { return engine_batch_; }
-
-  template <class F>
-  static void run(F&& f) {
-    try {
-      f();
-    } catch (const FoundationPoseError&) {
-      throw;
-    } catch (const std::exception& e) {
-      throw FoundationPoseError(e.what());
-    }
-  }
-
- private:
-  RuntimeOptions opts_;
-  Config cfg_;
-  int max_batch_;
-  int engine_batch_ = 0;
-  std::unique_ptr<fpb::NetworkRunner> net_;
 };
+
+TensorRtRunner::TensorRtRunner(RuntimeOptions options, Config config, int max_batch)
+    : impl_(std::make_unique<Impl>()) {
+  Impl& I = *impl_;
+  I.opts = std::move(options);
+  I.cfg = config;
+  I.max_batch = max_batch;
+  const int bs = config.batch_size > 0 ? config.batch_size : max_batch;
+  I.engine_batch = std::min(max_batch, bs);
+  if (I.engine_batch <= 0 || max_batch % I.engine_batch != 0) {
+    throw FoundationPoseError("max_batch (" + std::to_string(max_batch) + ") must be divisible by effective_bs (" +
+                              std::to_string(I.engine_batch) + ")");
+  }
+  checkCuda(cudaSetDevice(I.opts.device_id), "cudaSetDevice");
+}
+
+TensorRtRunner::~TensorRtRunner() = default;
+
+void TensorRtRunner::prepareForBatch(int batch_size) {
+  if (batch_size <= 0 || batch_size > impl_->max_batch) {
+    throw FoundationPoseError("prepare batch size exceeds configured maximum");
+  }
+  (void)impl_->net();
+}
+
+void TensorRtRunner::enqueueRefine(const float* rendered, const float* observed, float* dt, float* dr, int batch,
+                                   cudaStream_t stream) {
+  Impl& I = *impl_;
+  if (batch <= 0 || batch > I.max_batch) throw FoundationPoseError("refine batch size exceeds configured maximum");
+  const std::size_t stride = static_cast<std::size_t>(6) * I.cfg.input_width * I.cfg.input_height;
+  for (int off = 0; off < batch; off += I.engine_batch) {
+    const int chunk = std::min(I.engine_batch, batch - off);
+    I.net().loadNchw(rendered + off * stride, observed + off * stride, chunk, stream);
+    runNet([&] { I.net().refine(chunk, 0, dt + 3 * off, dr + 3 * off, stream); });
+  }
+}
+
+void TensorRtRunner::enqueueScore(const float* rendered, const float* observed, float* scores, int batch,
+                                  cudaStream_t stream) {
+  Impl& I = *impl_;
+  if (batch <= 0 || batch > I.max_batch) throw FoundationPoseError("score batch size exceeds configured maximum");
+  I.net().loadNchw(rendered, observed, batch, stream);
+  runNet([&] { I.net().score(batch, scores, stream); });
+}
 
 struct FoundationPose::Impl {
   PreprocessedMesh mesh;
@@ -371,7 +395,7 @@ struct FoundationPose::Impl {
   DeviceMesh dmesh;
   std::unique_ptr<IInferenceRunner> inference;
   std::unique_ptr<IRenderer> renderer;
-  BuiltinInferenceRunner* builtin_runner = nullptr;
+  TensorRtRunner::Impl* builtin_runner = nullptr;  // the built-in networks, when injected or default
   bool fused = false;  // built-in renderer + networks: fused render/pack path
   int rotation_count = 0;
   DeviceBuffer rgb, mask, depth_raw, depth_filtered, stats, rotations, poses, prev_pose, boxes;
@@ -426,7 +450,7 @@ struct FoundationPose::Impl {
                                  depth_filtered.as<float>(), w, h, toK(k), &params, mesh.diameter,
                                  cfg.depth_min, net.dtype(), net.stem().base, net.stem().plane_stride,
                                  boxes.as<float>() + 4 * off, render_ws.data(), render_ws.bytes(), s()));
-        BuiltinInferenceRunner::run(
+        runNet(
             [&] { net.refine(c, 0, dt.as<float>() + 3 * off, dr.as<float>() + 3 * off, s()); });
       }
     } else {
@@ -455,7 +479,7 @@ struct FoundationPose::Impl {
       fpkCheck(fpk_render_pack(&m, poses.as<float>(), n, rgb.as<uint8_t>(), depth_filtered.as<float>(),
                                w, h, toK(k), &params, mesh.diameter, 0.1f, net.dtype(), net.stem().base,
                                net.stem().plane_stride, boxes.as<float>(), render_ws.data(), render_ws.bytes(), s()));
-      BuiltinInferenceRunner::run([&] { net.score(n, scores.as<float>(), s()); });
+      runNet([&] { net.score(n, scores.as<float>(), s()); });
     } else {
       prepareSeamInputs(n, w, h, k, 0.1f);
       inference->enqueueScore(net_rendered.as<float>(), net_observed.as<float>(), scores.as<float>(), n, s());
@@ -507,7 +531,7 @@ struct FoundationPose::Impl {
     checkCuda(cudaMemcpyAsync(&host, flag, sizeof(int), cudaMemcpyDeviceToHost, s()), "read error flag");
     stream->synchronize();
     if (host != 0) {
-      BuiltinInferenceRunner::run([&] { builtin_runner->net().clearError(s()); });
+      runNet([&] { builtin_runner->net().clearError(s()); });
       stream->synchronize();
       throw FoundationPoseError("network kernel pipeline timed out (code " + std::to_string(host) + ")");
     }
@@ -543,7 +567,7 @@ int maxHypothesesFor(const Config& c) { return std::max(1, c.n_hypotheses); }
 
 FoundationPose::FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_options, Config config)
     : FoundationPose(std::move(mesh), runtime_options,
-                     std::make_unique<BuiltinInferenceRunner>(runtime_options, config, maxHypothesesFor(config)),
+                     std::make_unique<TensorRtRunner>(runtime_options, config, maxHypothesesFor(config)),
                      makeDefaultRenderer(config, runtime_options.device_id, maxHypothesesFor(config)),
                      config) {}
 
@@ -566,8 +590,8 @@ FoundationPose::FoundationPose(PreprocessedMesh mesh, RuntimeOptions runtime_opt
   I.stream = std::make_unique<CudaStream>();
   I.inference = std::move(inference_runner);
   I.renderer = std::move(renderer);
-  I.builtin_runner = dynamic_cast<BuiltinInferenceRunner*>(I.inference.get());
-  I.fused = I.builtin_runner != nullptr && dynamic_cast<BuiltinRenderer*>(I.renderer.get()) != nullptr;
+  if (auto* r = dynamic_cast<TensorRtRunner*>(I.inference.get())) I.builtin_runner = &r->impl();
+  I.fused = I.builtin_runner != nullptr && dynamic_cast<BuiltinRasterRenderer*>(I.renderer.get()) != nullptr;
 
   const std::size_t px = static_cast<std::size_t>(config.max_image_width) * config.max_image_height;
   if (px == 0 || config.input_width <= 0 || config.input_height <= 0) {
@@ -703,7 +727,7 @@ void FoundationPose::registerShardBegin(const std::uint8_t* rgb_u8, const float*
                            width, height, toK(intrinsics), &I.params, I.mesh.diameter, 0.1f, net.dtype(),
                            net.stem().base, net.stem().plane_stride, I.boxes.as<float>(), I.render_ws.data(),
                            I.render_ws.bytes(), I.s()));
-  BuiltinInferenceRunner::run([&] { net.scoreFeatures(shard_count, features, I.s()); });
+  runNet([&] { net.scoreFeatures(shard_count, features, I.s()); });
   checkCuda(cudaMemcpyAsync(poses, I.poses.data(), static_cast<std::size_t>(shard_count) * 64,
                             cudaMemcpyDeviceToDevice, I.s()),
             "cudaMemcpyAsync shard poses out");
@@ -719,7 +743,7 @@ PoseEstimate FoundationPose::registerShardFinish(const float* features, const fl
     throw FoundationPoseError("n_hypotheses must be in [1, " + std::to_string(I.max_hyp) + "]");
   }
   fpb::NetworkRunner& net = I.builtin_runner->net();
-  BuiltinInferenceRunner::run([&] { net.scoreHead(n_hypotheses, features, I.scores.as<float>(), I.s()); });
+  runNet([&] { net.scoreHead(n_hypotheses, features, I.scores.as<float>(), I.s()); });
   const float center[3] = {I.mesh.center.x, I.mesh.center.y, I.mesh.center.z};
   fpkCheck(fpk_select_best(poses, I.scores.as<float>(), n_hypotheses, center, I.best.as<float>(), I.s()));
   PoseEstimate e = I.readBest();
@@ -797,9 +821,95 @@ struct fp_handle {
   std::unique_ptr<FoundationPose> estimator;
 };
 
+namespace {
+
+// The group's host side: one long-lived worker thread per object, bound to
+// that object's device for its whole life (the estimator's stream, workspace
+// and graphs live there). A group call gives every active worker one job and
+// returns when all of them have finished, so a frame costs two condition-
+// variable hand-offs per object instead of a thread start and join (the
+// reference starts one std::jthread per object per call, c_api.cpp:203-237).
+class GroupWorkers {
+ public:
+  explicit GroupWorkers(const std::vector<int>& devices) : slots_(devices.size()) {
+    for (std::size_t i = 0; i < devices.size(); ++i) {
+      slots_[i].thread = std::thread([this, i, dev = devices[i]] { loop(slots_[i], dev); });
+    }
+  }
+  ~GroupWorkers() {
+    for (Slot& w : slots_) {
+      {
+        std::lock_guard<std::mutex> lock(w.mu);
+        w.stop = true;
+      }
+      w.cv.notify_one();
+    }
+    for (Slot& w : slots_) w.thread.join();
+  }
+  GroupWorkers(const GroupWorkers&) = delete;
+  GroupWorkers& operator=(const GroupWorkers&) = delete;
+
+  // Runs job(i) on worker i for every i with active[i]; errors[i] receives
+  // the message of a job that threw ("" when it returned).
+  void run(const std::vector<bool>& active, const std::function<void(std::size_t)>& job,
+           std::vector<std::string>& errors) {
+    std::ptrdiff_t n = 0;
+    for (bool a : active) n += a ? 1 : 0;
+    std::latch done(n);
+    for (std::size_t i = 0; i < slots_.size(); ++i) {
+      if (!active[i]) continue;
+      Slot& w = slots_[i];
+      {
+        std::lock_guard<std::mutex> lock(w.mu);
+        w.task = [&, i] {
+          try {
+            job(i);
+          } catch (const std::exception& e) {
+            errors[i] = e.what();
+            if (errors[i].empty()) errors[i] = "unknown error";
+          }
+          done.count_down();
+        };
+      }
+      w.cv.notify_one();
+    }
+    done.wait();
+  }
+
+ private:
+  struct Slot {
+    std::thread thread;
+    std::mutex mu;
+    std::condition_variable cv;
+    std::function<void()> task;
+    bool stop = false;
+  };
+
+  static void loop(Slot& w, int device) {
+    // Bind once; a job re-selects (and reports) the device if this failed.
+    if (cudaSetDevice(device) != cudaSuccess) cudaGetLastError();
+    for (;;) {
+      std::function<void()> task;
+      {
+        std::unique_lock<std::mutex> lock(w.mu);
+        w.cv.wait(lock, [&] { return w.stop || static_cast<bool>(w.task); });
+        if (!w.task) return;  // stop requested and nothing pending
+        task = std::move(w.task);
+        w.task = nullptr;
+      }
+      task();
+    }
+  }
+
+  std::vector<Slot> slots_;
+};
+
+}  // namespace
+
 struct fp_group {
   std::vector<std::unique_ptr<fp_handle>> handles;
   std::vector<int> device_ids;
+  std::unique_ptr<GroupWorkers> workers;  // declared last: stopped before the handles go
 };
 
 static_assert(sizeof(fp_config_t) == 14 * 4, "fp_config_t layout");
@@ -883,43 +993,59 @@ void writeResult(const PoseEstimate& e, fp_pose_result_t* r) {
   r->score = e.score;
 }
 
-// One worker thread per non-skipped object; each selects its object's device
-// (device selection is per thread) and runs `eval`. Returns the failure count;
-// the first failure message is tagged with the object index.
+// The C reference views (host buffers) as the estimator's view type; a NULL
+// camera_to_world is the identity (reference c_api.cpp fp_create_model_free).
+std::vector<ModelFreeReferenceView> referenceViews(const fp_reference_image_view_t* refs, size_t count) {
+  std::vector<ModelFreeReferenceView> views(count);
+  for (size_t i = 0; i < count; ++i) {
+    const fp_reference_image_view_t& r = refs[i];
+    if (r.k_row_major == nullptr) throw FoundationPoseError("Reference k_row_major is required");
+    ModelFreeReferenceView& v = views[i];
+    v.width = r.width;
+    v.height = r.height;
+    v.rgb_u8 = r.rgb_u8;
+    v.depth_m = r.depth_m;
+    v.mask_u8 = r.mask_u8;
+    v.intrinsics = CameraIntrinsics::fromRowMajor(r.k_row_major);
+    v.camera_to_world = Mat4f::identity();
+    if (r.camera_to_world_row_major != nullptr) {
+      std::copy(r.camera_to_world_row_major, r.camera_to_world_row_major + 16, v.camera_to_world.values.begin());
+    }
+  }
+  return views;
+}
+
+// A group call over the objects not skipped: per-object statuses, the number
+// of failures as the result and the first failure's message prefixed with its
+// object index (reference c_api.cpp:203-258 behaviour).
 int runGroup(fp_group* g, const std::vector<bool>& skip, fp_pose_result_t* results, int* statuses,
              char* err, size_t err_size, const std::function<PoseEstimate(FoundationPose&, size_t)>& eval) {
   const size_t n = g->handles.size();
-  std::vector<int> status(n, FP_OBJECT_OK);
+  std::vector<bool> active(n);
+  for (size_t i = 0; i < n; ++i) active[i] = !skip[i];
   std::vector<std::string> errors(n);
-  {
-    std::vector<std::jthread> workers;
-    for (size_t i = 0; i < n; ++i) {
-      if (skip[i]) {
-        status[i] = FP_OBJECT_SKIPPED;
-        continue;
-      }
-      workers.emplace_back([&, i] {
-        try {
-          const cudaError_t e = cudaSetDevice(g->device_ids[i]);
-          if (e != cudaSuccess) throw FoundationPoseError(cudaGetErrorString(e));
-          const PoseEstimate est = eval(*g->handles[i]->estimator, i);
-          if (results != nullptr) writeResult(est, results + i);
-        } catch (const std::exception& ex) {
-          status[i] = FP_OBJECT_FAILED;
-          errors[i] = ex.what();
-        }
-      });
+  std::vector<char> failed(n, 0);
+  g->workers->run(active, [&](size_t i) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != g->device_ids[i]) {
+      foundation_pose_nvidia::checkCuda(cudaSetDevice(g->device_ids[i]), "cudaSetDevice");
     }
-  }
+    try {
+      const PoseEstimate est = eval(*g->handles[i]->estimator, i);
+      if (results != nullptr) writeResult(est, results + i);
+    } catch (...) {
+      failed[i] = 1;
+      throw;
+    }
+  }, errors);
   int failures = 0;
+  std::string first;
   for (size_t i = 0; i < n; ++i) {
-    if (statuses != nullptr) statuses[i] = status[i];
-    if (status[i] == FP_OBJECT_FAILED) {
-      if (failures == 0) writeError(err, err_size, std::format("object {}: {}", i, errors[i]));
-      ++failures;
-    }
+    const int st = skip[i] ? FP_OBJECT_SKIPPED : (failed[i] ? FP_OBJECT_FAILED : FP_OBJECT_OK);
+    if (statuses != nullptr) statuses[i] = st;
+    if (st == FP_OBJECT_FAILED && failures++ == 0) first = std::format("object {}: {}", i, errors[i]);
   }
-  if (failures == 0) writeError(err, err_size, "");
+  writeError(err, err_size, first);
   return failures;
 }
 
@@ -967,23 +1093,7 @@ fp_handle_t* fp_create_model_free(const fp_reference_image_view_t* refs, size_t 
   try {
     if (refs == nullptr || count == 0) throw FoundationPoseError("At least one model-free reference image is required");
     if (options == nullptr) throw FoundationPoseError("create options are required");
-    std::vector<ModelFreeReferenceView> views;
-    for (size_t i = 0; i < count; ++i) {
-      const fp_reference_image_view_t& r = refs[i];
-      if (r.k_row_major == nullptr) throw FoundationPoseError("Reference k_row_major is required");
-      ModelFreeReferenceView v;
-      v.width = r.width;
-      v.height = r.height;
-      v.rgb_u8 = r.rgb_u8;
-      v.depth_m = r.depth_m;
-      v.mask_u8 = r.mask_u8;
-      v.intrinsics = CameraIntrinsics::fromRowMajor(r.k_row_major);
-      v.camera_to_world = Mat4f::identity();
-      if (r.camera_to_world_row_major != nullptr) {
-        for (int k = 0; k < 16; ++k) v.camera_to_world.values[static_cast<size_t>(k)] = r.camera_to_world_row_major[k];
-      }
-      views.push_back(v);
-    }
+    const std::vector<ModelFreeReferenceView> views = referenceViews(refs, count);
     auto h = std::make_unique<fp_handle>();
     h->estimator = std::make_unique<FoundationPose>(
         FoundationPose::createFromReferenceImages(views, toOptions(*options), toConfig(config)));
@@ -1081,6 +1191,7 @@ fp_group_t* fp_group_create(const fp_create_options_t* objects, size_t count, co
       g->handles.push_back(std::move(h));
       g->device_ids.push_back(objects[i].device_id);
     }
+    g->workers = std::make_unique<GroupWorkers>(g->device_ids);
     writeError(err, err_size, "");
     return g.release();
   } catch (const std::exception& e) {
@@ -1158,6 +1269,43 @@ int fp_synchronize_device(char* err, size_t err_size) {
   } catch (const std::exception& e) {
     writeError(err, err_size, e.what());
     return 1;
+  }
+}
+
+int fpk_model_free_mesh(const fp_reference_image_view_t* refs, size_t count, const fp_config_t* config,
+                        int* n_vertices, int* n_faces, float* vertices, uint8_t* colors, float* normals,
+                        int32_t* faces) {
+  try {
+    if (refs == nullptr || count == 0) throw FoundationPoseError("At least one model-free reference image is required");
+    if (n_vertices == nullptr || n_faces == nullptr) throw FoundationPoseError("fpk_model_free_mesh: count outputs are required");
+    const std::vector<ModelFreeReferenceView> views = referenceViews(refs, count);
+    const foundation_pose_nvidia::Mesh m = foundation_pose_nvidia::fpb_host::reconstructReferenceMesh(views, toConfig(config));
+    *n_vertices = static_cast<int>(m.vertices.size());
+    *n_faces = static_cast<int>(m.faces.size());
+    for (size_t i = 0; i < m.vertices.size(); ++i) {
+      if (vertices != nullptr) {
+        vertices[3 * i] = m.vertices[i].x;
+        vertices[3 * i + 1] = m.vertices[i].y;
+        vertices[3 * i + 2] = m.vertices[i].z;
+      }
+      if (colors != nullptr) {
+        colors[3 * i] = m.vertex_colors[i].r;
+        colors[3 * i + 1] = m.vertex_colors[i].g;
+        colors[3 * i + 2] = m.vertex_colors[i].b;
+      }
+      if (normals != nullptr) {
+        normals[3 * i] = m.normals[i].x;
+        normals[3 * i + 1] = m.normals[i].y;
+        normals[3 * i + 2] = m.normals[i].z;
+      }
+    }
+    if (faces != nullptr) {
+      for (size_t i = 0; i < m.faces.size(); ++i)
+        for (int k = 0; k < 3; ++k) faces[3 * i + k] = static_cast<int32_t>(m.faces[i][k]);
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    return fpb::fail(e.what());
   }
 }
 

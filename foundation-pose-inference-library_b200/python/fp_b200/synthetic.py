@@ -188,3 +188,34 @@ def render_frame_gpu(fpk, mesh: MeshData, normals: np.ndarray, pose: np.ndarray,
     rgb_u8 = (rgb.clamp(0, 1) * 255.0 + 0.5).to(torch.uint8).cpu().numpy()
     depth = xyz[..., 2].cpu().numpy().astype(np.float32)
     return rgb_u8, depth
+
+
+def fibonacci_directions(n: int) -> np.ndarray:
+    """n unit vectors spread evenly over the sphere (Fibonacci lattice)."""
+    i = np.arange(n) + 0.5
+    z = 1.0 - 2.0 * i / n
+    r = np.sqrt(np.maximum(0.0, 1.0 - z * z))
+    phi = np.pi * (3.0 - np.sqrt(5.0)) * i
+    return np.stack([r * np.cos(phi), r * np.sin(phi), z], 1)
+
+
+def look_at_origin(camera_position: np.ndarray) -> np.ndarray:
+    """camera_to_world (4x4, float32) of a camera at `camera_position` whose
+    optical axis (+z) points at the world origin, image rows (+y) downward."""
+    c = np.asarray(camera_position, np.float64)
+    z = -c / np.linalg.norm(c)
+    up = np.array([0.0, 0.0, 1.0]) if abs(z[2]) < 0.95 else np.array([0.0, 1.0, 0.0])
+    x = np.cross(z, up)
+    x /= np.linalg.norm(x)
+    y = np.cross(z, x)
+    m = np.eye(4)
+    m[:3, 0], m[:3, 1], m[:3, 2], m[:3, 3] = x, y, z, c
+    return m.astype(np.float32)
+
+
+def invert_pose(m: np.ndarray) -> np.ndarray:
+    out = np.eye(4, dtype=np.float64)
+    r = m[:3, :3].astype(np.float64)
+    out[:3, :3] = r.T
+    out[:3, 3] = -r.T @ m[:3, 3]
+    return out.astype(np.float32)

@@ -6,6 +6,7 @@
 #include <cstddef>
 #include <string>
 
+#pragma GCC visibility push(default)
 namespace foundation_pose_nvidia {
 
 // Network precision. kFP32 is strict IEEE fp32; kTF32/kFP16/kBF16 select the
@@ -76,3 +77,4 @@ struct RuntimeOptions {
 };
 
 }  // namespace foundation_pose_nvidia
+#pragma GCC visibility pop

@@ -1,18 +1,14 @@
-// RAII device memory and streams (reference include/foundation_pose_nvidia/device_buffer.hpp:14-44),
-// plus the FoundationPoseError exception (reference exception.hpp:18-21).
+// RAII device memory and streams (reference include/foundation_pose_nvidia/device_buffer.hpp:14-44).
 #pragma once
 
 #include <cuda_runtime_api.h>
 
 #include <cstddef>
-#include <stdexcept>
 
+#include "foundation_pose_nvidia/exception.hpp"
+
+#pragma GCC visibility push(default)
 namespace foundation_pose_nvidia {
-
-class FoundationPoseError : public std::runtime_error {
- public:
-  using std::runtime_error::runtime_error;
-};
 
 void checkCuda(cudaError_t status, const char* what);
 
@@ -57,3 +53,4 @@ class CudaStream {
 };
 
 }  // namespace foundation_pose_nvidia
+#pragma GCC visibility pop

@@ -12,14 +12,12 @@
 
 #include "foundation_pose_nvidia/config.hpp"
 #include "foundation_pose_nvidia/inference_runner.hpp"
+#include "foundation_pose_nvidia/mesh.hpp"
 #include "foundation_pose_nvidia/renderer.hpp"
 #include "foundation_pose_nvidia/types.hpp"
 
+#pragma GCC visibility push(default)
 namespace foundation_pose_nvidia {
-
-Mesh loadMesh(const std::filesystem::path& path);
-void computeVertexNormals(Mesh& mesh);
-PreprocessedMesh preprocessMesh(const Mesh& mesh, const Config& config);
 
 class FoundationPose {
  public:
@@ -76,3 +74,4 @@ class FoundationPose {
 };
 
 }  // namespace foundation_pose_nvidia
+#pragma GCC visibility pop

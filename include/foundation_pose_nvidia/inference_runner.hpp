@@ -5,6 +5,7 @@
 
 #include <cuda_runtime_api.h>
 
+#pragma GCC visibility push(default)
 namespace foundation_pose_nvidia {
 
 class IInferenceRunner {
@@ -18,3 +19,4 @@ class IInferenceRunner {
 };
 
 }  // namespace foundation_pose_nvidia
+#pragma GCC visibility pop

@@ -11,6 +11,7 @@
 #include "foundation_pose_nvidia/device_buffer.hpp"
 #include "foundation_pose_nvidia/types.hpp"
 
+#pragma GCC visibility push(default)
 namespace foundation_pose_nvidia {
 
 struct DeviceMesh {
@@ -41,3 +42,4 @@ class IRenderer {
 };
 
 }  // namespace foundation_pose_nvidia
+#pragma GCC visibility pop

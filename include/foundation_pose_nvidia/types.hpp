@@ -7,6 +7,7 @@
 #include <string>
 #include <vector>
 
+#pragma GCC visibility push(default)
 namespace foundation_pose_nvidia {
 
 struct Vec2f {
@@ -96,3 +97,4 @@ struct PoseEstimate {
 };
 
 }  // namespace foundation_pose_nvidia
+#pragma GCC visibility pop

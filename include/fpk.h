@@ -142,6 +142,19 @@ FP_API int fpk_load_mesh(const char* path, float mesh_unit_scale, int* n_vertice
                          float* vertices, float* normals, uint8_t* colors, int32_t* faces,
                          float* center3, float* diameter);
 
+/* Model-free object mesh from reference RGB-D views (host buffers), built on
+ * the current GPU. Replaces the reconstruction behind fp_create_model_free
+ * (reference src/foundation_pose.cpp:91-182): masked, valid depth samples on a
+ * stride lattice back-projected into the world frame, grid triangles with
+ * depth-continuous corners, area-weighted vertex normals; the mesh before
+ * centring. config supplies the model-free fields and the depth range (NULL =
+ * defaults). Call once with NULL arrays for the counts, then with arrays of
+ * n_vertices*3 floats (vertices, normals), n_vertices*3 bytes (colours) and
+ * n_faces*3 int32 (faces). */
+FP_API int fpk_model_free_mesh(const fp_reference_image_view_t* views, size_t count, const fp_config_t* config,
+                               int* n_vertices, int* n_faces, float* vertices, uint8_t* colors, float* normals,
+                               int32_t* faces);
+
 /* R <- exp(tanh(dr)*norm)^T R; t += dt*diameter/2. Replaces applyPoseDeltasOnDevice
  * (reference src/cuda_pipeline.cu:513-547, 847-858). In place. */
 FP_API int fpk_apply_deltas(float* poses, const float* delta_t, const float* delta_r, int n,

@@ -117,3 +117,46 @@ def write_obj(path, verts, faces, colors_u8) -> None:
                                                          enc(c[2])))
         for t in faces:
             f.write("f %d %d %d\n" % (t[0] + 1, t[1] + 1, t[2] + 1))
+
+
+def model_free_views(oracle, n_views: int, seed: int = 0, distance: float = 0.7, n_lat: int = 77,
+                     width: int = 640, height: int = 480):
+    """Reference views of a seeded displaced sphere (n_lat=77: 30,000 triangles)
+    from cameras on a Fibonacci sphere of radius `distance` looking at the
+    object (world frame = object frame). Returns (scene mesh parts, K, views
+    [(rgb u8, depth f32, mask u8)], camera_to_world list), rendered by the CPU
+    oracle."""
+    m = syn.displaced_sphere(seed, n_lat=n_lat, n_lon=200)
+    center, diameter, centered = oracle.mesh_center_diameter(m.vertices)
+    normals = oracle.vertex_normals(centered, m.faces)
+    colors_f = (m.colors.astype(np.float32) / np.float32(255.0)).astype(np.float32)
+    K = syn.K_640
+    k4 = np.array([K[0, 0], K[1, 1], K[0, 2], K[1, 2]], np.float32)
+    cfg = oracle.config(input_width=width, input_height=height)
+    boxes = np.array([[0.0, 0.0, float(width), float(height)]], np.float32)
+    views, c2ws = [], []
+    for d in syn.fibonacci_directions(n_views):
+        c2w = syn.look_at_origin(d * distance)
+        pose = syn.invert_pose(c2w)
+        rgb_f, xyz, _ = oracle.render(centered, normals, colors_f, m.faces, pose.reshape(1, 16), boxes, k4, cfg)
+        rgb = (np.clip(rgb_f[0], 0, 1) * 255.0 + 0.5).astype(np.uint8)
+        depth = xyz[0, ..., 2].astype(np.float32)
+        views.append((rgb, depth, (depth > 0).astype(np.uint8)))
+        c2ws.append(c2w)
+    parts = dict(verts=centered, normals=normals, colors_u8=m.colors, colors_f=colors_f, faces=m.faces,
+                 diameter=diameter, k4=k4)
+    return parts, K, views, c2ws
+
+
+def render_query(oracle, parts, pose, K, width: int = 640, height: int = 480, seed: int = 0,
+                 noise: float = 0.002, holes: float = 0.05):
+    """One query frame of the model-free object at `pose` (object -> camera)."""
+    rng = np.random.default_rng(seed)
+    cfg = oracle.config(input_width=width, input_height=height)
+    boxes = np.array([[0.0, 0.0, float(width), float(height)]], np.float32)
+    k4 = np.array([K[0, 0], K[1, 1], K[0, 2], K[1, 2]], np.float32)
+    rgb_f, xyz, _ = oracle.render(parts["verts"], parts["normals"], parts["colors_f"], parts["faces"],
+                                  np.asarray(pose, np.float32).reshape(1, 16), boxes, k4, cfg)
+    rgb = (np.clip(rgb_f[0], 0, 1) * 255.0 + 0.5).astype(np.uint8)
+    clean = xyz[0, ..., 2].astype(np.float32)
+    return rgb, syn.degrade_frame(rng, clean, noise, holes), (clean > 0).astype(np.uint8)
