@@ -64,18 +64,23 @@ def log(*a):
 # Scene
 # ---------------------------------------------------------------------------
 
-def build_scene(workdir: Path, seed: int):
-    from fp_b200 import synthetic as syn
-    from fp_b200.weights import make_default_packs
-
-    mesh = syn.displaced_sphere(seed)
-    obj = workdir / "object.obj"
-    with open(obj, "w") as f:
+def write_obj(path: Path, mesh) -> Path:
+    """OBJ with per-vertex colours that the loader maps back to the same u8 values."""
+    with open(path, "w") as f:
         for v, c in zip(mesh.vertices, mesh.colors):
             enc = [1.0 if x >= 255 else (float(x) + 0.5) / 255.0 for x in c]
             f.write("v %.9g %.9g %.9g %.9g %.9g %.9g\n" % (v[0], v[1], v[2], *enc))
         for t in mesh.faces:
             f.write("f %d %d %d\n" % (t[0] + 1, t[1] + 1, t[2] + 1))
+    return path
+
+
+def build_scene(workdir: Path, seed: int):
+    from fp_b200 import synthetic as syn
+    from fp_b200.weights import make_default_packs
+
+    mesh = syn.displaced_sphere(seed)
+    obj = write_obj(workdir / "object.obj", mesh)
     refine, score = make_default_packs(workdir / "weights", seed=0)
     rng = np.random.default_rng(seed + 17)
     gt = syn.random_pose(rng, dist=(0.65, 0.75), lateral=0.03)
@@ -239,7 +244,7 @@ def run_reference_arm(args) -> None:
 # Reference GPU baseline: the reference's own library on the same B200
 # ---------------------------------------------------------------------------
 
-REF_FULL_SO = ROOT / "oracle" / "_ref" / "libfpref_full.so"
+REF_FULL_SO = ROOT / "oracle" / "_ref" / "libfpref_full.so"  # baseline legs only
 
 
 def reference_gpu_baseline(obj, refine, score, rgb, depth, mask, K, steps: int, warmup: int, n_hyp: int,
@@ -524,6 +529,345 @@ def kernel_track(args) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# The other BASELINE configurations
+# ---------------------------------------------------------------------------
+
+def _render(fpk, mesh, pose, K, w, h, rng, noise, holes):
+    """Frame of `mesh` at `pose` rendered by the library's rasterizer (the whole
+    frame as the crop), depth degraded by Gaussian noise and zeroed holes; the
+    mask comes from the clean depth."""
+    from fp_b200 import synthetic as syn
+
+    normals = syn.vertex_normals(mesh.vertices, mesh.faces)
+    rgb, depth = syn.render_frame_gpu(fpk, mesh, normals, pose, K, w, h)
+    mask = (depth > 0).astype(np.uint8)
+    return rgb, syn.degrade_frame(rng, depth, noise, holes), mask
+
+
+def _timed(torch, fn, steps: int) -> float:
+    """ms per call of fn over `steps` calls, CUDA events on the current stream
+    bracketing synchronous calls."""
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def config_stress(args, world: int, rank: int, local: int) -> dict:
+    """register under micro-batching stress -- a seeded 250k-triangle
+    mesh (mostly sub-pixel triangles), 1280x720 frame (fx=fy=900, cx=640,
+    cy=360) with 20% depth holes, 252 hypotheses, 5 refinement passes,
+    batch_size 42, BF16; sharded over the ranks like the headline register."""
+    import torch
+
+    from fp_b200 import synthetic as syn
+    from fp_b200.capi import FP_PRECISION_BF16, SCORE_FEATURE_DIM, Api, image_view
+    from fp_b200.dist_utils import barrier, max_over_ranks
+    from fp_b200.kernels import FpkLibrary
+    from fp_b200.sharded import gather_shards, shard_range
+    from fp_b200.weights import make_default_packs
+
+    work = Path(tempfile.mkdtemp(prefix=f"fpbench_c3_{rank}_"))
+    mesh = syn.dense_mesh(args.seed)
+    obj = write_obj(work / "dense.obj", mesh)
+    refine, score = make_default_packs(work / "weights", seed=0)
+    rng = np.random.default_rng(args.seed + 31)
+    gt = syn.random_pose(rng, dist=(0.65, 0.75), lateral=0.03)
+    rgb, depth, mask = _render(FpkLibrary(), mesh, gt, syn.K_1280, 1280, 720, rng, 0.002, 0.2)
+    api = Api()
+    cfg = api.default_config(n_hypotheses=N_HYP, n_refine_iters=N_ITERS, batch_size=42,
+                             tensorrt_precision=FP_PRECISION_BF16, capture_cuda_graph=False,
+                             max_image_width=1280, max_image_height=720)
+    h = api.create(Api.options(obj, refine, score, local, work), cfg)
+    api.prepare(h, N_HYP)
+    dev = torch.device("cuda", local)
+    view = image_view(*(torch.from_numpy(x).to(dev) for x in (rgb, depth)), syn.K_1280,
+                      torch.from_numpy(mask).to(dev))
+    begin, count = shard_range(N_HYP, world, rank)
+    rows = -(-N_HYP // world)
+    feats = torch.zeros((rows, SCORE_FEATURE_DIM), device=dev)
+    poses = torch.zeros((rows, 16), device=dev)
+
+    def register():
+        if world == 1:
+            api.register(h, view)
+            return
+        api.shard_begin(h, view, -1, N_HYP, begin, count, feats.data_ptr(), poses.data_ptr())
+        f, p = gather_shards(feats, N_HYP), gather_shards(poses, N_HYP)
+        torch.cuda.synchronize(dev)
+        api.shard_finish(h, f.data_ptr(), p.data_ptr(), N_HYP)
+
+    for _ in range(max(3, args.warmup)):
+        register()
+    barrier()
+    ms = max_over_ranks(_timed(torch, register, max(3, args.steps // 2)), dev)
+    fpk = FpkLibrary()
+    fpk.lib.fpk_profile_enable.argtypes = [C.c_int]
+    fpk.lib.fpk_profile_read.argtypes = [C.c_void_p] * 4
+    fpk.lib.fpk_profile_reset()
+    fpk.lib.fpk_profile_enable(1)
+    register()
+    torch.cuda.synchronize()
+    fpk.lib.fpk_profile_enable(0)
+    ms_st, work_st = (C.c_double * 5)(), (C.c_double * 5)()
+    fpk.lib.fpk_profile_read(ms_st, work_st, None, None)
+    api.destroy(h)
+    render_s = ms_st[1] / 1000.0
+    return {"workload": "configs[2]: register, 250k-tri mesh (sub-pixel triangles), 1280x720, 20% depth holes, "
+                        "252 hyp, 5 iters, batch_size 42, BF16",
+            "n_gpus": world, "register_ms": ms, "hyp_per_s": N_HYP / (ms / 1000.0),
+            "micro_batches": "42 per RefineNet launch" + ("" if world == 1 else
+                                                           f"; shards of {count} refine in 42 + remainder"),
+            "faces": int(mesh.faces.shape[0]),
+            "render_ms_per_register": ms_st[1], "gemm_ms_per_register": ms_st[0],
+            "triangles_per_s": (6 * count * mesh.faces.shape[0] / render_s) if render_s > 0 else None,
+            "stage_note": "stage split from one eager register on rank 0's shard with per-stage CUDA events"}
+
+
+def config_track(args, reference: bool) -> dict:
+    """track at FP32 -- icosphere (subdivision 5, 20,480 triangles)
+    scaled to a 0.10 x 0.07 x 0.05 m ellipsoid with random u8 vertex colours,
+    640x480 (fx=fy=600), 100 frames of a seeded random walk (0.6-1.0 m,
+    <= 2 cm and <= 5 deg per frame), depth noise 2 mm, 5% zeroed; register on
+    the first frame, then 2-iteration track per frame (B = 1). FP32 runs
+    TF32 tensor-core products with fp32 accumulation."""
+    import torch
+
+    from fp_b200 import synthetic as syn
+    from fp_b200.capi import FP_PRECISION_FP32, Api, image_view
+    from fp_b200.kernels import FpkLibrary
+    from fp_b200.weights import make_default_packs
+
+    work = Path(tempfile.mkdtemp(prefix="fpbench_c1_"))
+    mesh = syn.ellipsoid_mesh(args.seed, subdivisions=5, extent=(0.10, 0.07, 0.05))
+    obj = write_obj(work / "ellipsoid.obj", mesh)
+    refine, score = make_default_packs(work / "weights", seed=0)
+    rng = np.random.default_rng(args.seed + 7)
+    pose = syn.random_pose(rng, dist=(0.6, 1.0), lateral=0.03)
+    fpk = FpkLibrary()
+    frames = []
+    for _ in range(101):
+        frames.append(_render(fpk, mesh, pose, syn.K_640, W, H, rng, 0.002, 0.05))
+        pose = syn.random_walk(rng, pose, max_t=0.02, max_deg=5.0)
+        pose[2, 3] = np.clip(pose[2, 3], 0.6, 1.0)
+    dev = torch.device("cuda", 0)
+    d_frames = [tuple(torch.from_numpy(x).to(dev) for x in f) for f in frames]
+    p_frames = [tuple(torch.from_numpy(x).pin_memory() for x in f) for f in frames]
+    api = Api()
+    cfg = api.default_config(n_hypotheses=N_HYP, batch_size=N_HYP, tensorrt_precision=FP_PRECISION_FP32,
+                             capture_cuda_graph=args.graph, max_image_width=W, max_image_height=H)
+    h = api.create(Api.options(obj, refine, score, 0, work), cfg)
+    reg = image_view(d_frames[0][0], d_frames[0][1], syn.K_640, d_frames[0][2])
+    dev_views = [image_view(f[0], f[1], syn.K_640) for f in d_frames[1:]]
+    host_views = [image_view(f[0], f[1], syn.K_640) for f in p_frames[1:]]
+
+    def run(views):
+        api.register(h, reg)
+        for _ in range(3):
+            api.track(h, views[0])
+        it = iter(range(len(views)))
+        return _timed(torch, lambda: api.track(h, views[next(it)]), len(views))
+
+    ms = run(dev_views)
+    e2e_ms = run(host_views)
+    api.destroy(h)
+    out = {"workload": "configs[0]: track, icosphere-5 ellipsoid 0.10x0.07x0.05 m, 640x480, 100-frame random walk, "
+                       "2 iterations, B=1, FP32 (TF32 tensor-core products)",
+           "track_hz": 1000.0 / ms, "ms_per_frame": ms, "e2e_track_hz": 1000.0 / e2e_ms,
+           "h2d_bytes_per_frame": int(frames[0][0].nbytes + frames[0][1].nbytes), "d2h_bytes_per_frame": 68,
+           "cuda_graph": bool(args.graph)}
+    if reference and REF_FULL_SO.is_file():
+        out["reference_gpu"] = reference_track(obj, refine, score, d_frames, syn.K_640)
+        if out["reference_gpu"].get("track_hz"):
+            out["reference_gpu"]["speedup_track"] = out["track_hz"] / out["reference_gpu"]["track_hz"]
+    return out
+
+
+def reference_track(obj, refine, score, d_frames, K) -> dict:
+    """BASELINE leg for configs[0]: the reference library's own fp_track_frame
+    (oracle/_ref/libfpref_full.so) at FP32 with torch fp32 networks (TF32
+    off, cuDNN, CUDA-graph replay) on the same device-resident frames."""
+    import torch
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from fp_b200 import capi
+    from fp_b200.weights import read_pack
+    from fp_net_torch import TorchNets, install
+
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    lib = C.CDLL(str(REF_FULL_SO))
+    for name, (res, argt) in capi._SIGNATURES.items():
+        if hasattr(lib, name):
+            getattr(lib, name).restype, getattr(lib, name).argtypes = res, argt
+    nets = TorchNets(read_pack(refine)[1], read_pack(score)[1], torch.float32)
+    callbacks = install(lib, nets)  # noqa: F841
+    cfg = capi.fp_config_t()
+    lib.fp_default_config(C.byref(cfg))
+    cfg.n_hypotheses, cfg.batch_size, cfg.tensorrt_precision = N_HYP, N_HYP, capi.FP_PRECISION_FP32
+    cfg.max_image_width, cfg.max_image_height = W, H
+    opts = capi.Api.options(obj, refine, score, 0, None)
+    err = C.create_string_buffer(4096)
+    h = lib.fp_create(C.byref(opts), C.byref(cfg), err, len(err))
+    if not h:
+        return {"unavailable": f"reference fp_create failed: {err.value.decode()}"}
+    res = capi.fp_pose_result_t()
+    try:
+        reg = capi.image_view(d_frames[0][0], d_frames[0][1], K, d_frames[0][2])
+        if lib.fp_register_frame(h, C.byref(reg), -1, -1, C.byref(res), err, len(err)) != 0:
+            return {"unavailable": f"reference register failed: {err.value.decode()}"}
+        views = [capi.image_view(f[0], f[1], K) for f in d_frames[1:]]
+        for v in views[:3]:
+            lib.fp_track_frame(h, C.byref(v), -1, C.byref(res), err, len(err))
+        it = iter(range(len(views)))
+
+        def step():
+            if lib.fp_track_frame(h, C.byref(views[next(it)]), -1, C.byref(res), err, len(err)) != 0:
+                raise RuntimeError(err.value.decode())
+
+        ms = _timed(torch, step, len(views))
+    finally:
+        lib.fp_destroy(h)
+    return {"track_hz": 1000.0 / ms, "ms_per_frame": ms,
+            "networks": "torch fp32 (TF32 off), cuDNN, CUDA-graph replay (stand-in for TensorRT FP32 engines)"}
+
+
+def config_model_free(args) -> dict:
+    """model-free register then track -- 16 reference views
+    (640x480 RGB-D + mask) of a seeded 30k-triangle object from a 16-point
+    Fibonacci sphere at 0.7 m; fp_create_model_free, register (252
+    hypotheses, 5 passes), then a 200-frame random walk tracked; TF32."""
+    import torch
+
+    from fp_b200 import synthetic as syn
+    from fp_b200.capi import FP_PRECISION_TF32, Api, image_view, reference_view
+    from fp_b200.kernels import FpkLibrary
+    from fp_b200.weights import make_default_packs
+
+    work = Path(tempfile.mkdtemp(prefix="fpbench_c4_"))
+    mesh = syn.displaced_sphere(args.seed, n_lat=77, n_lon=200)  # 30,000 triangles
+    refine, score = make_default_packs(work / "weights", seed=0)
+    fpk = FpkLibrary()
+    rng = np.random.default_rng(args.seed + 3)
+    views = []
+    for d in syn.fibonacci_directions(16):
+        c2w = syn.look_at_origin(d * 0.7)
+        rgb, depth, mask = _render(fpk, mesh, syn.invert_pose(c2w), syn.K_640, W, H, rng, 0.0, 0.0)
+        views.append(reference_view(rgb, depth, mask, syn.K_640, c2w))
+    pose = syn.random_pose(rng, dist=(0.6, 0.8), lateral=0.03)
+    frames = []
+    for _ in range(201):
+        frames.append(_render(fpk, mesh, pose, syn.K_640, W, H, rng, 0.002, 0.05))
+        pose = syn.random_walk(rng, pose)
+    dev = torch.device("cuda", 0)
+    d_frames = [tuple(torch.from_numpy(x).to(dev) for x in f) for f in frames]
+    api = Api()
+    cfg = api.default_config(n_hypotheses=N_HYP, batch_size=N_HYP, tensorrt_precision=FP_PRECISION_TF32,
+                             capture_cuda_graph=args.graph, max_image_width=W, max_image_height=H)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    h = api.create_model_free(views, Api.options(None, refine, score, 0, work), cfg)
+    create_s = time.perf_counter() - t0
+    reg = image_view(d_frames[0][0], d_frames[0][1], syn.K_640, d_frames[0][2])
+    for _ in range(2):
+        api.register(h, reg)
+    reg_ms = _timed(torch, lambda: api.register(h, reg), max(3, args.steps // 2))
+    tviews = [image_view(f[0], f[1], syn.K_640) for f in d_frames[1:]]
+    it = iter(range(len(tviews)))
+    track_ms = _timed(torch, lambda: api.track(h, tviews[next(it)]), len(tviews))
+    api.destroy(h)
+    return {"metric": "model-free register ms and track Hz (configs[3], TF32)", "n_gpus": 1,
+            "create_model_free_s": create_s, "register_ms": reg_ms, "hyp_per_s": N_HYP / (reg_ms / 1000.0),
+            "track_hz": 1000.0 / track_ms, "track_frames": len(tviews), "views": 16, "dtype": "tf32",
+            "data": "synthetic (seeded 30k-triangle object; random-init weights)", "cuda_graph": bool(args.graph)}
+
+
+def config_group(args) -> dict:
+    """eight seeded meshes of 20k-100k triangles in one shared
+    1280x720 RGB-D frame with per-object masks, fp_group_* with the objects
+    placed round-robin over the visible GPUs (one object per GPU at 8 GPUs):
+    a group register (252 hypotheses, 5 passes each), then 300 group-tracked
+    frames (2 passes); FP16. Frames are host buffers (one camera, every GPU
+    uploads its own copy)."""
+    import torch
+
+    from fp_b200 import synthetic as syn
+    from fp_b200.capi import FP_PRECISION_FP16, Api, image_view
+    from fp_b200.kernels import FpkLibrary
+    from fp_b200.weights import make_default_packs
+
+    n_dev = min(torch.cuda.device_count(), args.gpus)
+    work = Path(tempfile.mkdtemp(prefix="fpbench_c5_"))
+    refine, score = make_default_packs(work / "weights", seed=0)
+    rng = np.random.default_rng(args.seed + 5)
+    meshes, objs, poses = [], [], []
+    for i in range(8):
+        faces = int(20000 + 80000 * i / 7)
+        n_lat = faces // 400 + 2
+        m = syn.displaced_sphere(args.seed + i, n_lat=n_lat, n_lon=200, radius=0.035)
+        meshes.append(m)
+        objs.append(write_obj(work / f"object{i}.obj", m))
+        p = syn.random_pose(rng, dist=(0.8, 1.0), lateral=0.0)
+        p[0, 3], p[1, 3] = (i % 4 - 1.5) * 0.16, (i // 4 - 0.5) * 0.18
+        poses.append(p)
+    fpk = FpkLibrary()
+
+    def composite(poses_now, noise_rng):
+        """One shared frame: every object rendered alone, nearest surface wins."""
+        rgb = np.zeros((720, 1280, 3), np.uint8)
+        depth = np.zeros((720, 1280), np.float32)
+        owner = np.full((720, 1280), -1, np.int32)
+        for i, (m, p) in enumerate(zip(meshes, poses_now)):
+            normals = syn.vertex_normals(m.vertices, m.faces)
+            r, d = syn.render_frame_gpu(fpk, m, normals, p, syn.K_1280, 1280, 720)
+            front = (d > 0) & ((depth == 0) | (d < depth))
+            rgb[front], depth[front], owner[front] = r[front], d[front], i
+        masks = [(owner == i).astype(np.uint8) for i in range(8)]
+        return rgb, syn.degrade_frame(noise_rng, depth, 0.002, 0.05), masks
+
+    rgb, depth, masks = composite(poses, rng)
+    frames = []
+    walk = [p.copy() for p in poses]
+    for _ in range(300):
+        walk = [syn.random_walk(rng, p) for p in walk]
+        frames.append(composite(walk, rng)[:2])
+    api = Api()
+    cfg = api.default_config(n_hypotheses=N_HYP, batch_size=N_HYP, tensorrt_precision=FP_PRECISION_FP16,
+                             capture_cuda_graph=args.graph, max_image_width=1280, max_image_height=720)
+    opts = [Api.options(o, refine, score, i % n_dev, work) for i, o in enumerate(objs)]
+    g = api.group_create(opts, cfg)
+    try:
+        view = image_view(rgb, depth, syn.K_1280)
+        fails, *_ = api.group_register(g, view, masks)
+        assert fails == 0
+        t0 = time.perf_counter()
+        steps = max(2, args.steps // 4)
+        for _ in range(steps):
+            fails, *_rest, err = api.group_register(g, view, masks)
+            assert fails == 0, err
+        reg_ms = (time.perf_counter() - t0) * 1000.0 / steps
+        tviews = [image_view(r, d, syn.K_1280) for r, d in frames]
+        api.group_track(g, tviews[0], None, 8)
+        t0 = time.perf_counter()
+        for v in tviews:
+            fails, *_rest, err = api.group_track(g, v, None, 8)
+            assert fails == 0, err
+        track_s = time.perf_counter() - t0
+    finally:
+        api.lib.fp_group_destroy(g)
+    return {"metric": "group register ms and tracked object-frames/s (configs[4], 8 objects, FP16)",
+            "n_gpus": n_dev, "objects": 8, "placement": "object i on GPU i mod n_gpus",
+            "group_register_ms": reg_ms, "register_hyp_per_s": 8 * N_HYP / (reg_ms / 1000.0),
+            "group_track_hz": len(tviews) / track_s, "object_frames_per_s": 8 * len(tviews) / track_s,
+            "timing": "host wall clock around each synchronous group call (host frames, H2D inside)",
+            "faces": [int(m.faces.shape[0]) for m in meshes], "dtype": "f16", "cuda_graph": bool(args.graph)}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 
@@ -550,6 +894,8 @@ def main() -> None:
     ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
                     help="skip the reference-library GPU baseline (oracle/_ref/libfpref_full.so + torch networks)")
     ap.add_argument("--track-frames", type=int, default=50)
+    ap.add_argument("--no-configs", dest="configs", action="store_false",
+                    help="skip the configs[2] stress register and the configs[0] FP32 track measurements")
     ap.add_argument("--e2e-steps", type=int, default=None, help="host-buffer steps (default: --steps)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="capture_cuda_graph=0; by default the refinement pass replays as one CUDA graph "
@@ -557,6 +903,9 @@ def main() -> None:
     ap.add_argument("--hyp", type=int, default=252,
                     help="hypotheses per register; values other than 252 are for profiling captures only "
                          "(the workload line then names the reduced count)")
+    ap.add_argument("--config", choices=["model-free", "group", "track"], default=None,
+                    help="measure one of the other BASELINE configurations alone (one process; group spreads its "
+                         "objects over --gpus visible GPUs) and print its JSON line")
     ap.add_argument("--kernel", choices=["gemm", "render", "refine", "track"], default=None,
                     help="time one hot-path stage alone (tuning / ncu captures) instead of the register step")
     ap.add_argument("--batch", type=int, default=128, help="--kernel: images / hypotheses per launch")
@@ -570,6 +919,14 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--pairs", type=int, default=1, choices=[0, 1])
     args = ap.parse_args()
+    if args.config is not None:
+        import torch
+
+        torch.cuda.set_device(0)
+        fn = {"model-free": config_model_free, "group": config_group,
+              "track": lambda a: config_track(a, a.reference_gpu)}[args.config]
+        print(json.dumps(fn(args)), flush=True)
+        return
     if args.kernel is not None:
         fn = {"gemm": kernel_gemm, "render": kernel_render, "refine": kernel_refine, "track": kernel_track}[args.kernel]
         print(json.dumps(fn(args)), flush=True)
@@ -727,7 +1084,11 @@ def main() -> None:
         track_hz = args.track_frames / (time.perf_counter() - t0)
     api.destroy(h)
 
+    # configs[2] (stress, sharded like the headline register: every rank takes part).
+    stress = config_stress(args, world, rank, local) if args.configs else None
+
     if rank == 0:
+        track_c1 = config_track(args, args.reference_gpu) if (args.configs and world == 1) else None
         pk = peaks()
         gemm_ms, gemm_flops, gemm_n = ms_tot[0], work_tot[0], timed[0]
         achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
@@ -787,6 +1148,7 @@ def main() -> None:
             "clocks": clocks,
             "cpu_baseline": cpu_base,
             "reference_gpu": ref_gpu,
+            "configs": {"c3_stress": stress, "c1_track": track_c1},
             "pose_host_equals_device": None if pose_host is None else bool(np.array_equal(pose_dev, pose_host)),
         }
         print(json.dumps(line), flush=True)

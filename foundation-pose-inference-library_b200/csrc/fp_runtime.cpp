@@ -709,7 +709,11 @@ void FoundationPose::registerShardBegin(const std::uint8_t* rgb_u8, const float*
                               std::to_string(shard_begin + shard_count) + ") is outside the " +
                               std::to_string(active) + " active hypotheses");
   }
-  const int eff = refineChunk(I, shard_count);
+  // The reference's batch rules apply to the register as a whole (all active
+  // hypotheses); a shard then refines in micro-batches of that size counted
+  // from its own first hypothesis, the last one possibly shorter (a 63-
+  // hypothesis shard of a batch-42 register runs 42 + 21).
+  const int eff = std::min(refineChunk(I, active), shard_count);
   I.upload(rgb_u8, depth_m, mask_u8, width, height);
   fpkCheck(fpk_preprocess(I.depth_raw.as<float>(), I.mask.as<uint8_t>(), width, height, toK(intrinsics),
                           &I.params, I.depth_filtered.as<float>(), nullptr, nullptr, I.stats.as<int32_t>(), I.s()));

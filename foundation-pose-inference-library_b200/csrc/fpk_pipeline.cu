@@ -697,8 +697,12 @@ __device__ __forceinline__ void storeS2d(void* net, long long plane_stride, int 
     // record (KP4), so channels 0-3 go to plane 2*sub and 4-7 to plane 2*sub+1.
     unsigned char* d0 = reinterpret_cast<unsigned char*>(net) + (2 * sub) * plane_stride +
                         ((static_cast<long long>(img) * gh + gy) * gw + gx) * 16;
-    *reinterpret_cast<float4*>(d0) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(d0 + plane_stride) = make_float4(v[4], v[5], 0.0f, 0.0f);
+    // The stem reads fp32 inputs as TF32: round to nearest here, as every other
+    // producer of a TF32 operand does (the NCHW seam loader included).
+    *reinterpret_cast<float4*>(d0) =
+        make_float4(tc::tf32Round(v[0]), tc::tf32Round(v[1]), tc::tf32Round(v[2]), tc::tf32Round(v[3]));
+    *reinterpret_cast<float4*>(d0 + plane_stride) =
+        make_float4(tc::tf32Round(v[4]), tc::tf32Round(v[5]), 0.0f, 0.0f);
     (void)dst;
   }
 }

@@ -119,7 +119,8 @@ FP_API int fpk_pack(const uint8_t* rgb, const float* depth_filtered, int width, 
  * (y, x) of image i (rendered i = 0..n-1, observed n+i) goes to plane
  * ((y+3)%2)*2 + (x+3)%2, row i*gh*gw + ((y+3)/2)*gw + (x+3)/2 with
  * gh = (H+7)/2, gw = (W+7)/2 (83 x 83 for 160 x 160 crops): 16 bytes = 6 values
- * + 2 zeros of `dtype`. net_input points at row 0 of plane 0; planes are
+ * + 2 zeros of `dtype` (fp32 values rounded to nearest TF32, the precision the
+ * tensor cores read them at; two records per pixel for fp32). net_input points at row 0 of plane 0; planes are
  * plane_stride bytes apart. Rows never written (the zero border of the grid)
  * must be zero before first use. Replaces the computeCropBoxes ->
  * IRenderer::render -> prepareNetworkInputs sequence (reference

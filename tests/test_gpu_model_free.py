@@ -90,13 +90,15 @@ def rot_err_deg(a, b):
 
 
 def test_model_free_register_track_matches_reference_library(oracle, tmp_path):
-    """configs[3] at test size: 16 views, TF32, 42 hypotheses, 2 refinement
-    passes, then 3 tracked frames of a seeded random walk."""
+    """configs[3] at test size: 16 views, TF32, a register refined from the
+    first rotation of the grid (one hypothesis: with random-init weights the
+    ScoreNet scores of different hypotheses tie to within rounding, so a
+    many-hypothesis arg-max would compare tie-breaks rather than poses), 2
+    refinement passes, then 3 tracked frames of a seeded random walk."""
     if not reflib_util.REF_FULL_SO.is_file():
         pytest.skip("reference library build not present")
     refine, score = make_default_packs(tmp_path, seed=11)
-    scores = {}
-    ref = reflib_util.load(read_pack(refine)[1], read_pack(score)[1], keep_scores=scores)
+    ref = reflib_util.load(read_pack(refine)[1], read_pack(score)[1])
     rl = ref["lib"]
     parts, K, views, c2ws = model_free_views(oracle, 16, seed=4)
     api = capi.Api()
@@ -117,8 +119,8 @@ def test_model_free_register_track_matches_reference_library(oracle, tmp_path):
             view = capi.image_view(rgb, depth, K, mask if step == 0 else None)
             res = capi.fp_pose_result_t()
             if step == 0:
-                ours, score_ours = api.register(h, view, 2, -1)
-                assert rl.fp_register_frame(rh, C.byref(view), 2, -1, C.byref(res), err, len(err)) == 0, \
+                ours, score_ours = api.register(h, view, 2, 1)
+                assert rl.fp_register_frame(rh, C.byref(view), 2, 1, C.byref(res), err, len(err)) == 0, \
                     err.value.decode()
             else:
                 ours, score_ours = api.track(h, view, 2)
@@ -129,10 +131,7 @@ def test_model_free_register_track_matches_reference_library(oracle, tmp_path):
             print(f"model-free step {step}: dt={t_err:.4f} mm dR={r_err:.4f} deg, score {score_ours:.5f} vs "
                   f"{res.score:.5f}")
             if step == 0:
-                s = np.sort(scores["scores"])[::-1]
                 assert abs(score_ours - res.score) <= 1e-3 * max(1.0, abs(res.score))
-                if (s[0] - s[1]) / max(1.0, abs(s[0])) <= 1e-3:
-                    pytest.skip("the reference's two best register scores tie within the network tolerance")
             assert t_err <= 1.0 and r_err <= 0.1
             pose = syn.random_walk(rng, pose)
     finally:
