@@ -633,8 +633,9 @@ def config_track(args, reference: bool) -> dict:
     scaled to a 0.10 x 0.07 x 0.05 m ellipsoid with random u8 vertex colours,
     640x480 (fx=fy=600), 100 frames of a seeded random walk (0.6-1.0 m,
     <= 2 cm and <= 5 deg per frame), depth noise 2 mm, 5% zeroed; register on
-    the first frame, then 2-iteration track per frame (B = 1). FP32 runs
-    TF32 tensor-core products with fp32 accumulation."""
+    the first frame, then 2-iteration track per frame (B = 1). FP32 is
+    strict: every layer sums three TF32 products of split operands and the
+    attention runs in fp32 FMA arithmetic."""
     import torch
 
     from fp_b200 import synthetic as syn
@@ -676,7 +677,7 @@ def config_track(args, reference: bool) -> dict:
     e2e_ms = run(host_views)
     api.destroy(h)
     out = {"workload": "configs[0]: track, icosphere-5 ellipsoid 0.10x0.07x0.05 m, 640x480, 100-frame random walk, "
-                       "2 iterations, B=1, FP32 (TF32 tensor-core products)",
+                       "2 iterations, B=1, FP32 (strict: split-operand TF32 GEMMs, fp32 attention)",
            "track_hz": 1000.0 / ms, "ms_per_frame": ms, "e2e_track_hz": 1000.0 / e2e_ms,
            "h2d_bytes_per_frame": int(frames[0][0].nbytes + frames[0][1].nbytes), "d2h_bytes_per_frame": 68,
            "cuda_graph": bool(args.graph)}

@@ -265,7 +265,11 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
       for (int b = k_issued > G::kKSlots ? k_issued - G::kKSlots : 0; b < k_issued; ++b) {
         drainBar(&bars->k_full[b % G::kKSlots], (b / G::kKSlots) & 1);
       }
-      for (int b = v_issued > 2 ? v_issued - 2 : 0; b < v_issued; ++b) {
+      // fp32 stages V through one buffer: only the last block can still be in
+      // flight, and an earlier block's parity already names a later phase of
+      // the same barrier (waiting on it would only end at the timeout).
+      const int v_in_flight = G::kTf32 ? 1 : 2;
+      for (int b = v_issued > v_in_flight ? v_issued - v_in_flight : 0; b < v_issued; ++b) {
         if (G::kTf32) {
           drainBar(&bars->v_full[0], b & 1);
         } else {
@@ -543,6 +547,8 @@ cudaError_t launchAttentionTc(const AttnArgs& a, int layers, int n_seq, int dtyp
       return attn::launch<__nv_bfloat16>(a, layers, n_seq, s);
     case FPK_DTYPE_F32:
       return attn::launch<float>(a, layers, n_seq, s);
+    case FPK_DTYPE_F32_EXACT:
+      return launchAttentionExact(a, layers, n_seq, s);
     default:
       return attn::launch<__half>(a, layers, n_seq, s);
   }
@@ -561,10 +567,10 @@ extern "C" int fpk_attention(const void* qkv, long long qkv_plane_stride, int qk
                              long long out_plane_stride, int out_layer_channels, int layers, int heads,
                              int seq_len, int n_seq, int dtype, int* error_flag, void* stream) {
   if (qkv == nullptr || out == nullptr || error_flag == nullptr) return fpb::fail("fpk_attention: null pointer");
-  if (dtype != FPK_DTYPE_F16 && dtype != FPK_DTYPE_BF16 && dtype != FPK_DTYPE_F32) {
-    return fpb::fail("fpk_attention: dtype must be f16, bf16 or f32");
+  if (dtype != FPK_DTYPE_F16 && dtype != FPK_DTYPE_BF16 && dtype != FPK_DTYPE_F32 && dtype != FPK_DTYPE_F32_EXACT) {
+    return fpb::fail("fpk_attention: dtype must be f16, bf16, f32 or f32-exact");
   }
-  const int per = dtype == FPK_DTYPE_F32 ? 4 : 8;
+  const int per = (dtype == FPK_DTYPE_F32 || dtype == FPK_DTYPE_F32_EXACT) ? 4 : 8;
   if (seq_len <= 0 || n_seq <= 0 || layers <= 0 || heads <= 0 || qkv_layer_channels % per ||
       q_channel % per || k_channel % per || v_channel % per || out_layer_channels % per) {
     return fpb::fail("fpk_attention: bad sizes");

@@ -196,15 +196,21 @@ __device__ __forceinline__ void unpackRec8(const uint4* in, float* v) {
 
 template <typename T>
 __device__ __forceinline__ void storeRec8(unsigned char* base, long long plane_stride, int c,
-                                          long long row, const float* v) {
+                                          long long row, const float* v, bool exact) {
   constexpr int kP = Elem<T>::kPerRecord;
   unsigned char* q = base + static_cast<long long>(c / kP) * plane_stride + row * 16;
   if constexpr (Elem<T>::kTf32) {
+    if (exact) {  // FPK_DTYPE_F32_EXACT: the value as accumulated
+      *reinterpret_cast<float4*>(q) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(q + plane_stride) = make_float4(v[4], v[5], v[6], v[7]);
+      return;
+    }
     // fp32 outputs are the next layer's TF32 operands: round to nearest here.
     *reinterpret_cast<float4*>(q) = make_float4(tf32Round(v[0]), tf32Round(v[1]), tf32Round(v[2]), tf32Round(v[3]));
     *reinterpret_cast<float4*>(q + plane_stride) =
         make_float4(tf32Round(v[4]), tf32Round(v[5]), tf32Round(v[6]), tf32Round(v[7]));
   } else {
+    (void)exact;
     *reinterpret_cast<uint4*>(q) = pack8<T>(v);
   }
 }
@@ -270,7 +276,8 @@ __device__ __forceinline__ void finish8(const fpk_gemm_desc_t& d, const RowDst& 
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
   }
-  storeRec8<T>(static_cast<unsigned char*>(d.dst), d.dst_plane_stride, rd.ch_base + n, rd.drow, v);
+  storeRec8<T>(static_cast<unsigned char*>(d.dst), d.dst_plane_stride, rd.ch_base + n, rd.drow, v,
+               d.dtype == FPK_DTYPE_F32_EXACT);
 }
 
 // Split-K partial sums: split ks of output tile mn is a [BN/4][128][4] fp32
@@ -885,13 +892,14 @@ int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map
   EncodeTiledFn enc = encodeFn();
   if (enc == nullptr) return fail("fpk_gemm: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kprime), static_cast<cuuint64_t>(d.cout)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kprime) * (d.dtype == FPK_DTYPE_F32 ? 4 : 2)};
-  const int esize = d.dtype == FPK_DTYPE_F32 ? 4 : 2;
+  const bool f32 = d.dtype == FPK_DTYPE_F32 || d.dtype == FPK_DTYPE_F32_EXACT;
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kprime) * (f32 ? 4 : 2)};
+  const int esize = f32 ? 4 : 2;
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(kStageBytes / esize), static_cast<cuuint32_t>(bn)};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map,
                          d.dtype == FPK_DTYPE_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                         : d.dtype == FPK_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                         : f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                          2, const_cast<void*>(d.w), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1076,10 +1084,11 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     return fail("fpk_gemm: null pointer in descriptor");
   }
   const fpk_gemm_desc_t& d = *desc;
-  if (d.dtype != FPK_DTYPE_F16 && d.dtype != FPK_DTYPE_BF16 && d.dtype != FPK_DTYPE_F32) {
-    return fail("fpk_gemm: dtype must be f16, bf16 or f32 (TF32 tensor-core math)");
+  if (d.dtype != FPK_DTYPE_F16 && d.dtype != FPK_DTYPE_BF16 && d.dtype != FPK_DTYPE_F32 &&
+      d.dtype != FPK_DTYPE_F32_EXACT) {
+    return fail("fpk_gemm: dtype must be f16, bf16, f32 or f32-exact (TF32 tensor-core math)");
   }
-  const int esize = d.dtype == FPK_DTYPE_F32 ? 4 : 2;
+  const int esize = (d.dtype == FPK_DTYPE_F32 || d.dtype == FPK_DTYPE_F32_EXACT) ? 4 : 2;
   const int stage_elems = kStageBytes / esize;  // 64 (16-bit) or 32 (fp32) channels per chunk
   if (d.taps < 1 || d.taps > FPK_GEMM_MAX_TAPS) return fail("fpk_gemm: taps out of range");
   if (d.cin < 32 || (d.cin != 32 && d.cin % stage_elems != 0)) {
@@ -1193,6 +1202,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
                  : bn == 128 ? launchPair<__nv_bfloat16, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
                              : launchPair<__nv_bfloat16, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
         case FPK_DTYPE_F32:
+        case FPK_DTYPE_F32_EXACT:
           return bn == 256   ? launchPair<float, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
                  : bn == 128 ? launchPair<float, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
                              : launchPair<float, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
@@ -1236,6 +1246,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     case FPK_DTYPE_BF16:
       return launchShape<__nv_bfloat16>(d, pl, map, smem, s, bn, mh);
     case FPK_DTYPE_F32:
+    case FPK_DTYPE_F32_EXACT:
       return launchShape<float>(d, pl, map, smem, s, bn, mh);
     default:
       return launchShape<__half>(d, pl, map, smem, s, bn, mh);

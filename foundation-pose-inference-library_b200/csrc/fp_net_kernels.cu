@@ -47,10 +47,21 @@ __device__ __forceinline__ __half cvt<__half>(float v) { return __float2half_rn(
 template <>
 __device__ __forceinline__ float cvt<float>(float v) { return tc::tf32Round(v); }
 
+// Conversion of a produced activation: kExact keeps fp32 values as computed
+// (FPK_DTYPE_F32_EXACT, the strict-FP32 networks), else cvt<T>.
+template <typename T, bool kExact>
+__device__ __forceinline__ T cvtOut(float v) {
+  if constexpr (kExact && sizeof(T) == 4) {
+    return v;
+  } else {
+    return cvt<T>(v);
+  }
+}
+
 // LayerNorm over 512 channels (eps inside the sqrt, biased variance, affine)
 // for R rows per CTA, planar in/out: 16-byte records of 8 (fp16/bf16) or 4
 // (fp32) channels.
-template <typename T, int R>
+template <typename T, int R, bool kExact = false>
 __global__ void __launch_bounds__(256) layerNormKernel(LnArgs a) {
   tc::pdlTrigger();
   tc::pdlWait();
@@ -95,7 +106,7 @@ __global__ void __launch_bounds__(256) layerNormKernel(LnArgs a) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int ch = lane * 16 + i;
-      tile[row][ch] = cvt<T>((v[i] - mean) * rstd * a.gamma[ch] + a.beta[ch]);
+      tile[row][ch] = cvtOut<T, kExact>((v[i] - mean) * rstd * a.gamma[ch] + a.beta[ch]);
     }
   }
   __syncthreads();
@@ -367,7 +378,7 @@ __global__ void __launch_bounds__(128) smallAttentionKernel(const float* __restr
 }
 
 // NCHW fp32 [n][6][H][W] (rendered, observed) -> stem space-to-depth KP8.
-template <typename T>
+template <typename T, bool kExact = false>
 __global__ void nchwToStemKernel(const float* __restrict__ rendered, const float* __restrict__ observed,
                                  int n, int H, int W, unsigned char* __restrict__ dst,
                                  long long plane_stride) {
@@ -382,7 +393,9 @@ __global__ void nchwToStemKernel(const float* __restrict__ rendered, const float
   const long long plane = static_cast<long long>(H) * W;
   alignas(16) T v[8];
 #pragma unroll
-  for (int c = 0; c < 6; ++c) v[c] = cvt<T>(src[(static_cast<long long>(s) * 6 + c) * plane + static_cast<long long>(y) * W + x]);
+  for (int c = 0; c < 6; ++c) {
+    v[c] = cvtOut<T, kExact>(src[(static_cast<long long>(s) * 6 + c) * plane + static_cast<long long>(y) * W + x]);
+  }
   v[6] = cvt<T>(0.0f);
   v[7] = cvt<T>(0.0f);
   const int gw = (W + 7) / 2;
@@ -398,6 +411,28 @@ __global__ void nchwToStemKernel(const float* __restrict__ rendered, const float
     *reinterpret_cast<uint4*>(dst + (sub * kRecs + q) * plane_stride + row) =
         reinterpret_cast<const uint4*>(v)[q];
   }
+}
+
+// Strict-FP32 operand split of a KP4 planar activation: hi = x rounded to
+// nearest TF32, lo = (x - hi) rounded to nearest TF32, over every row of the
+// window [-pre, rows + post) of every plane (rows outside the activation's
+// range are copied as they are, so the guard rows read by shifted
+// convolution windows stay as the source has them). Three TF32 products
+// hi*W_hi + hi*W_lo + lo*W_hi recover an fp32-accurate product (the dropped
+// lo*W_lo term and the roundings are below fp32 rounding of the sum).
+__global__ void splitTf32Kernel(const float4* __restrict__ src, long long src_stride, float4* __restrict__ hi,
+                                float4* __restrict__ lo, long long dst_stride, long long rows, int planes, int pre,
+                                int post) {
+  const long long span = rows + pre + post;
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= span * planes) return;
+  const int p = static_cast<int>(i / span);
+  const long long r = i - static_cast<long long>(p) * span - pre;
+  const float4 x = src[p * (src_stride / 16) + r];
+  const float4 h = make_float4(tc::tf32Round(x.x), tc::tf32Round(x.y), tc::tf32Round(x.z), tc::tf32Round(x.w));
+  hi[p * (dst_stride / 16) + r] = h;
+  lo[p * (dst_stride / 16) + r] = make_float4(tc::tf32Round(x.x - h.x), tc::tf32Round(x.y - h.y),
+                                              tc::tf32Round(x.z - h.z), tc::tf32Round(x.w - h.w));
 }
 
 // fp32 -> half-precision copy (weights).
@@ -418,6 +453,9 @@ cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s) {
       return launchPdl(layerNorm16Kernel<__nv_bfloat16>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
     case FPK_DTYPE_F32:
       return launchPdl(layerNormKernel<float, 16>, dim3(static_cast<unsigned>((a.rows + 15) / 16)), dim3(256), 0, s, a);
+    case FPK_DTYPE_F32_EXACT:
+      return launchPdl(layerNormKernel<float, 16, true>, dim3(static_cast<unsigned>((a.rows + 15) / 16)), dim3(256), 0,
+                       s, a);
     default:
       return launchPdl(layerNorm16Kernel<__half>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
   }
@@ -430,6 +468,7 @@ cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int
     case FPK_DTYPE_BF16:
       return launchPdl(tokenMeanKernel<__nv_bfloat16>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
     case FPK_DTYPE_F32:
+    case FPK_DTYPE_F32_EXACT:
       return launchPdl(tokenMeanKernel<float>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
     default:
       return launchPdl(tokenMeanKernel<__half>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
@@ -465,9 +504,22 @@ cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n
     case FPK_DTYPE_F32:
       nchwToStemKernel<float><<<grid, 256, 0, s>>>(rendered, observed, n, H, W, d, plane_stride);
       break;
+    case FPK_DTYPE_F32_EXACT:
+      nchwToStemKernel<float, true><<<grid, 256, 0, s>>>(rendered, observed, n, H, W, d, plane_stride);
+      break;
     default:
       nchwToStemKernel<__half><<<grid, 256, 0, s>>>(rendered, observed, n, H, W, d, plane_stride);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launchSplitTf32(const unsigned char* src, long long src_stride, unsigned char* hi, unsigned char* lo,
+                            long long dst_stride, long long rows, int planes, int pre, int post, cudaStream_t s) {
+  prof::countLaunch(prof::kOther);
+  const long long total = (rows + pre + post) * planes;
+  splitTf32Kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(src), src_stride, reinterpret_cast<float4*>(hi),
+      reinterpret_cast<float4*>(lo), dst_stride, rows, planes, pre, post);
   return cudaGetLastError();
 }
 

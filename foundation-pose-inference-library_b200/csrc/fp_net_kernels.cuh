@@ -58,6 +58,13 @@ cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStre
 cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n, int H, int W,
                              void* dst, long long plane_stride, int dtype, cudaStream_t s);
 cudaError_t launchConvert(const float* in, void* out, long long n, bool bf16, cudaStream_t s);
+// Strict-FP32 operand split (fp_net_kernels.cu splitTf32Kernel): src, hi, lo
+// point at row 0 of plane 0 of KP4 planar buffers; rows [-pre, rows + post).
+cudaError_t launchSplitTf32(const unsigned char* src, long long src_stride, unsigned char* hi, unsigned char* lo,
+                            long long dst_stride, long long rows, int planes, int pre, int post, cudaStream_t s);
+// fp32 FMA self-attention (fp_attention_exact.cu) for FPK_DTYPE_F32_EXACT, same
+// arguments and layout as launchAttentionTc with KP4 records.
+cudaError_t launchAttentionExact(const AttnArgs& a, int layers, int n_seq, cudaStream_t s);
 
 }  // namespace net
 }  // namespace fpb

@@ -15,6 +15,7 @@
 // LayerNorm + token mean; ScoreNet's cross-hypothesis attention is fp32.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -254,9 +255,18 @@ class Network {
     return static_cast<float*>(p);
   }
 
+  // Strict FP32: the part of each weight below its TF32 rounding, itself
+  // rounded to TF32 (the hi * W_lo product of the three-term split).
+  void* uploadWeightRemainder(const std::vector<float>& v) {
+    const std::vector<float> hi = roundTf32(v);
+    std::vector<float> lo(v.size());
+    for (size_t i = 0; i < v.size(); ++i) lo[i] = v[i] - hi[i];
+    return upload(roundTf32(lo));
+  }
+
   // Weights in the activation type: fp32 as is, else converted on the device.
   void* uploadWeights(const std::vector<float>& v) {
-    if (dtype_ == FPK_DTYPE_F32) return upload(roundTf32(v));
+    if (dtype_ == FPK_DTYPE_F32 || dtype_ == FPK_DTYPE_F32_EXACT) return upload(roundTf32(v));
     float* tmp = nullptr;
     check(cudaMalloc(&tmp, v.size() * 4), "cudaMalloc staging");
     check(cudaMemcpy(tmp, v.data(), v.size() * 4, cudaMemcpyHostToDevice), "upload staging");
@@ -274,7 +284,9 @@ class Network {
             int cout, int cin, int taps, const std::vector<int>& offs, double flops_per_row) {
     ConvLayer c;
     c.flops_per_row = flops_per_row;
-    c.w = uploadWeights(chunkMajor(taps_w, cout, taps, cin, chunk()));
+    const std::vector<float> cm = chunkMajor(taps_w, cout, taps, cin, chunk());
+    c.w = uploadWeights(cm);
+    if (dtype_ == FPK_DTYPE_F32_EXACT) c.w_lo = uploadWeightRemainder(cm);
     c.bias = upload(pack.at(name + ".b"));
     c.cin = cin;
     c.cout = cout;
@@ -292,7 +304,9 @@ class Network {
 
   ConvLayer linear(const std::vector<float>& w, const std::vector<float>& b, int cout, int cin) {
     ConvLayer c;
-    c.w = uploadWeights(chunkMajor(w, cout, 1, cin, chunk()));
+    const std::vector<float> cm = chunkMajor(w, cout, 1, cin, chunk());
+    c.w = uploadWeights(cm);
+    if (dtype_ == FPK_DTYPE_F32_EXACT) c.w_lo = uploadWeightRemainder(cm);
     c.bias = upload(b);
     c.cin = cin;
     c.cout = cout;
@@ -301,7 +315,7 @@ class Network {
     return c;
   }
 
-  int chunk() const { return dtype_ == FPK_DTYPE_F32 ? 32 : 64; }
+  int chunk() const { return (dtype_ == FPK_DTYPE_F32 || dtype_ == FPK_DTYPE_F32_EXACT) ? 32 : 64; }
 
   int dtype_;
   std::vector<void*>& allocs_;
@@ -389,6 +403,23 @@ NetworkRunner::NetworkRunner(const std::string& refine_path, const std::string& 
     allocations_.push_back(e);
     check(cudaMemset(e, 0, 16), "zero error flag");
     err_ = static_cast<int*>(e);
+    if (dt == FPK_DTYPE_F32_EXACT) {
+      // Largest split activation (a GEMM input: x1, 2B images x 41^2 rows x
+      // 256 channels) and partial sum (a GEMM output on its input's grid: the
+      // RefineNet QKV output, B x 400 rows x 3072 channels, or the stem's 64
+      // channels on the 83^2 grid).
+      auto planar_bytes = [](long long rows, int channels) {
+        return static_cast<size_t>(((kGuardPre + rows + kGuardPost) * 16 + 255) / 256 * 256) * (channels / 4);
+      };
+      split_bytes_ = std::max(planar_bytes(N * kG40 * kG40, 256), planar_bytes(N * kStemGrid * kStemGrid, 32));
+      split_bytes_ = std::max(split_bytes_, planar_bytes(B * kG20 * kG20, 1024));
+      partial_bytes_ = std::max(planar_bytes(N * kStemGrid * kStemGrid, 64), planar_bytes(B * kTokens, 6 * kEmbed));
+      for (void** p : {&split_hi_, &split_lo_, &partial_[0], &partial_[1]}) {
+        const size_t bytes = (p == &split_hi_ || p == &split_lo_) ? split_bytes_ : partial_bytes_;
+        check(cudaMalloc(p, bytes), "cudaMalloc strict-FP32 scratch");
+        allocations_.push_back(*p);
+      }
+    }
     splitk_bytes_ = 24ll << 20;
     check(cudaMalloc(&splitk_, static_cast<size_t>(splitk_bytes_)), "cudaMalloc split-K scratch");
     allocations_.push_back(splitk_);
@@ -411,12 +442,16 @@ int NetworkRunner::dtype() const {
       return FPK_DTYPE_BF16;
     case NetPrecision::kFP16:
       return FPK_DTYPE_F16;
+    case NetPrecision::kTF32:
+      return FPK_DTYPE_F32;  // fp32 activations rounded to TF32, TF32 tensor-core products
     default:
-      return FPK_DTYPE_F32;  // FP32 and TF32: fp32 activations, TF32 tensor-core math
+      return FPK_DTYPE_F32_EXACT;  // FP32: fp32 activations, split-operand products (fp32-accurate)
   }
 }
 
-int NetworkRunner::perRecord() const { return dtype() == FPK_DTYPE_F32 ? 4 : 8; }
+int NetworkRunner::perRecord() const {
+  return (dtype() == FPK_DTYPE_F32 || dtype() == FPK_DTYPE_F32_EXACT) ? 4 : 8;
+}
 
 void NetworkRunner::gemm(const ConvLayer& L, const Planar& a, long long a_row0, long long rows,
                          const Planar& dst, int mode, int img_rows, int grid_w, int valid_h,
@@ -454,7 +489,63 @@ void NetworkRunner::gemm(const ConvLayer& L, const Planar& a, long long a_row0, 
   d.splitk_ws_bytes = split_k_ ? splitk_bytes_ : 0;
   const double valid_rows = static_cast<double>(rows / img_rows) * valid_h * valid_w;
   prof::Scope scope(prof::kGemm, valid_rows * L.flops_per_row, s);
+  if (d.dtype == FPK_DTYPE_F32_EXACT) {
+    exactGemm(d, L, s);
+    return;
+  }
   if (fpk_gemm(&d, s) != 0) throw std::runtime_error(fpk_last_error());
+}
+
+// Strict FP32 layer: A is split into TF32 hi and lo parts, and the layer is
+//   P1  = A_hi W_hi + bias + residual        (SAME layout on A's grid)
+//   P2  = A_hi W_lo + P1
+//   out = A_lo W_hi + P2, then ReLU / destination layout / embedding,
+// every partial kept in fp32. The dropped A_lo W_lo term is below 2^-20 of
+// the product, so the result carries fp32 accuracy (the reference's FP32
+// engines run fp32 arithmetic, src/tensorrt_runner.cu:65-80).
+void NetworkRunner::exactGemm(const fpk_gemm_desc_t& d, const ConvLayer& L, cudaStream_t s) {
+  auto stride_for = [](long long rows) { return ((kGuardPre + rows + kGuardPost) * 16 + 255) / 256 * 256; };
+  const int a_planes = d.cin / 4;
+  const long long a_stride = stride_for(d.rows);
+  const long long p_stride = stride_for(d.rows);
+  if (static_cast<size_t>(a_stride) * a_planes > split_bytes_ ||
+      static_cast<size_t>(p_stride) * (d.cout / 4) > partial_bytes_) {
+    throw std::runtime_error("strict-FP32 scratch too small for a layer");
+  }
+  unsigned char* hi = static_cast<unsigned char*>(split_hi_) + kGuardPre * 16;
+  unsigned char* lo = static_cast<unsigned char*>(split_lo_) + kGuardPre * 16;
+  check(net::launchSplitTf32(static_cast<const unsigned char*>(d.a), d.a_plane_stride, hi, lo, a_stride, d.rows,
+                             a_planes, static_cast<int>(kGuardPre), static_cast<int>(kGuardPost), s),
+        "split operands");
+  unsigned char* p1 = static_cast<unsigned char*>(partial_[0]) + kGuardPre * 16;
+  unsigned char* p2 = static_cast<unsigned char*>(partial_[1]) + kGuardPre * 16;
+  fpk_gemm_desc_t g = d;
+  // P1: A_hi W_hi + bias + residual.
+  g.a = hi;
+  g.a_plane_stride = a_stride;
+  g.w = L.w;
+  g.relu = 0;
+  g.dst = p1;
+  g.dst_plane_stride = p_stride;
+  g.dst_mode = FPK_DST_SAME;
+  g.pos = nullptr;
+  if (fpk_gemm(&g, s) != 0) throw std::runtime_error(fpk_last_error());
+  // P2: A_hi W_lo + P1.
+  g.w = L.w_lo;
+  g.bias = nullptr;
+  g.residual = p1;
+  g.res_plane_stride = p_stride;
+  g.dst = p2;
+  if (fpk_gemm(&g, s) != 0) throw std::runtime_error(fpk_last_error());
+  // out: A_lo W_hi + P2 through the layer's own epilogue.
+  g = d;
+  g.a = lo;
+  g.a_plane_stride = a_stride;
+  g.w = L.w;
+  g.bias = nullptr;
+  g.residual = p2;
+  g.res_plane_stride = p_stride;
+  if (fpk_gemm(&g, s) != 0) throw std::runtime_error(fpk_last_error());
 }
 
 // Encoder for n hypotheses whose 2n images start at stem row `stem_row0`;

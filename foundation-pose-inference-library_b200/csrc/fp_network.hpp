@@ -43,6 +43,7 @@ enum class NetPrecision { kFP32 = 0, kTF32 = 1, kFP16 = 2, kBF16 = 3 };
 
 struct ConvLayer {
   void* w = nullptr;       // [cout][K'] in the activation type, chunk-major
+  void* w_lo = nullptr;    // strict FP32: the weights' TF32 remainder (w - w rounded), same layout
   float* bias = nullptr;   // [cout]
   int cin = 0, cout = 0, taps = 0;
   int tap_off[FPK_GEMM_MAX_TAPS] = {};
@@ -115,6 +116,14 @@ class NetworkRunner {
   void* splitk_ = nullptr;
   long long splitk_bytes_ = 0;
   bool split_k_ = false;
+  // Strict FP32 (precision kFP32): each layer runs as three TF32 GEMMs of
+  // split operands, hi*W_hi + hi*W_lo + lo*W_hi; the split activation and the
+  // two partial sums live here (bytes each; 0 for the other precisions).
+  void* split_hi_ = nullptr;
+  void* split_lo_ = nullptr;
+  void* partial_[2] = {nullptr, nullptr};
+  size_t split_bytes_ = 0, partial_bytes_ = 0;
+  void exactGemm(const fpk_gemm_desc_t& d, const ConvLayer& L, cudaStream_t s);
 };
 
 }  // namespace fpb

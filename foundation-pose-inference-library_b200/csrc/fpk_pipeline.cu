@@ -344,7 +344,7 @@ constexpr int kSmallTriPixels = 32;
 constexpr int kRasterThreads = 256;
 constexpr int kBigTriThreads = 256;
 
-enum class RenderOut { kNhwc = 0, kS2dF32 = 1, kS2dF16 = 2, kS2dBf16 = 3 };
+enum class RenderOut { kNhwc = 0, kS2dF32 = 1, kS2dF16 = 2, kS2dBf16 = 3, kS2dF32Exact = 4 };
 
 struct RenderArgs {
   fpk_mesh_t mesh;
@@ -677,7 +677,7 @@ __device__ __forceinline__ __nv_bfloat16 fromFloat<__nv_bfloat16>(float v) {
 // 8 channels (6 used + 2 zero) of one crop pixel into the stem's
 // space-to-depth KP8 layout: pixel (y, x) -> plane ((y+3)%2)*2 + (x+3)%2, row
 // of grid cell ((y+3)/2, (x+3)/2). See fp_nets.cu for how the stem consumes it.
-template <typename T>
+template <typename T, bool kExact = false>
 __device__ __forceinline__ void storeS2d(void* net, long long plane_stride, int img, int y, int x,
                                          int gw, int gh, const float* v) {
   const int gy = (y + 3) >> 1;
@@ -697,12 +697,17 @@ __device__ __forceinline__ void storeS2d(void* net, long long plane_stride, int 
     // record (KP4), so channels 0-3 go to plane 2*sub and 4-7 to plane 2*sub+1.
     unsigned char* d0 = reinterpret_cast<unsigned char*>(net) + (2 * sub) * plane_stride +
                         ((static_cast<long long>(img) * gh + gy) * gw + gx) * 16;
-    // The stem reads fp32 inputs as TF32: round to nearest here, as every other
-    // producer of a TF32 operand does (the NCHW seam loader included).
-    *reinterpret_cast<float4*>(d0) =
-        make_float4(tc::tf32Round(v[0]), tc::tf32Round(v[1]), tc::tf32Round(v[2]), tc::tf32Round(v[3]));
-    *reinterpret_cast<float4*>(d0 + plane_stride) =
-        make_float4(tc::tf32Round(v[4]), tc::tf32Round(v[5]), 0.0f, 0.0f);
+    if constexpr (kExact) {  // strict FP32: the stem splits its operands itself
+      *reinterpret_cast<float4*>(d0) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(d0 + plane_stride) = make_float4(v[4], v[5], 0.0f, 0.0f);
+    } else {
+      // The stem reads fp32 inputs as TF32: round to nearest here, as every other
+      // producer of a TF32 operand does (the NCHW seam loader included).
+      *reinterpret_cast<float4*>(d0) =
+          make_float4(tc::tf32Round(v[0]), tc::tf32Round(v[1]), tc::tf32Round(v[2]), tc::tf32Round(v[3]));
+      *reinterpret_cast<float4*>(d0 + plane_stride) =
+          make_float4(tc::tf32Round(v[4]), tc::tf32Round(v[5]), 0.0f, 0.0f);
+    }
     (void)dst;
   }
 }
@@ -864,11 +869,12 @@ __global__ void __launch_bounds__(kShadeThreads) shadeKernel(RenderArgs a) {
     if (a.tri_ids != nullptr) a.tri_ids[idx] = tri_plus_one;
   } else {
     const PackedPixel pk = packPixel(a, hs, px, y, width, height, rgb, xyz, lut255);
+    constexpr bool kExact = kOut == RenderOut::kS2dF32Exact;
     using T = typename std::conditional<
-        kOut == RenderOut::kS2dF32, float,
+        kOut == RenderOut::kS2dF32 || kExact, float,
         typename std::conditional<kOut == RenderOut::kS2dF16, __half, __nv_bfloat16>::type>::type;
-    storeS2d<T>(a.net, a.plane_stride, hyp, y, px, a.grid_w, a.grid_h, pk.r);
-    storeS2d<T>(a.net, a.plane_stride, a.n + hyp, y, px, a.grid_w, a.grid_h, pk.o);
+    storeS2d<T, kExact>(a.net, a.plane_stride, hyp, y, px, a.grid_w, a.grid_h, pk.r);
+    storeS2d<T, kExact>(a.net, a.plane_stride, a.n + hyp, y, px, a.grid_w, a.grid_h, pk.o);
   }
 }
 
@@ -1108,7 +1114,9 @@ int launchRender(RenderArgs& a, void* workspace, size_t workspace_bytes, cudaStr
   // Algorithmic bytes: mesh once, the frame once (rgb + depth) when packing,
   // and the outputs (NHWC fp32 rgb+xyz, or both packed network inputs).
   const double px = static_cast<double>(a.n) * a.p.input_width * a.p.input_height;
-  const double elt = kOut == RenderOut::kNhwc ? 0.0 : (kOut == RenderOut::kS2dF32 ? 4.0 : 2.0);
+  const double elt = kOut == RenderOut::kNhwc
+                         ? 0.0
+                         : ((kOut == RenderOut::kS2dF32 || kOut == RenderOut::kS2dF32Exact) ? 4.0 : 2.0);
   const double bytes = a.mesh.n_vertices * 36.0 + a.mesh.n_faces * 12.0 +
                        (kOut == RenderOut::kNhwc ? px * 24.0
                                                  : px * 12.0 * elt + a.img_w * static_cast<double>(a.img_h) * 7.0);
@@ -1301,6 +1309,8 @@ int fpk_render_pack(const fpk_mesh_t* mesh, const float* poses, int n, const uin
   switch (dtype) {
     case FPK_DTYPE_F32:
       return launchRender<RenderOut::kS2dF32>(a, workspace, workspace_bytes, s);
+    case FPK_DTYPE_F32_EXACT:
+      return launchRender<RenderOut::kS2dF32Exact>(a, workspace, workspace_bytes, s);
     case FPK_DTYPE_F16:
       return launchRender<RenderOut::kS2dF16>(a, workspace, workspace_bytes, s);
     case FPK_DTYPE_BF16:

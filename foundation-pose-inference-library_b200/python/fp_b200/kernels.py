@@ -16,6 +16,7 @@ LIB_PATH = PKG / "lib" / "libfoundation_pose_nvidia.so"
 FPK_DTYPE_F32 = 0
 FPK_DTYPE_F16 = 1
 FPK_DTYPE_BF16 = 2
+FPK_DTYPE_F32_EXACT = 3  # fp32 kept exact (strict-FP32 networks)
 FPK_STATS_INTS = 8 + 65536
 
 

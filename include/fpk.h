@@ -57,6 +57,11 @@ typedef struct fpk_mesh {
 #define FPK_DTYPE_F32 0
 #define FPK_DTYPE_F16 1
 #define FPK_DTYPE_BF16 2
+/* fp32 kept exact: values are stored without rounding to TF32. fpk_gemm still
+ * multiplies on the tensor cores as TF32 (it is the building block of the
+ * exact-FP32 layers, which sum three TF32 products of split operands);
+ * fpk_attention runs fp32 FMA arithmetic; fpk_render_pack stores plain fp32. */
+#define FPK_DTYPE_F32_EXACT 3
 
 /* Size in int32 of the translation-statistics scratch (bbox, count, 65,536-bin histogram). */
 #define FPK_STATS_INTS (8 + 65536)

@@ -11,13 +11,16 @@ import pytest
 
 torch = pytest.importorskip("torch")
 
-from fp_b200.kernels import FPK_DTYPE_BF16, FPK_DTYPE_F16, FPK_DTYPE_F32, attention  # noqa: E402
+from fp_b200.kernels import FPK_DTYPE_BF16, FPK_DTYPE_F16, FPK_DTYPE_F32, FPK_DTYPE_F32_EXACT, attention  # noqa: E402
 from kp8_util import Planar  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16, FPK_DTYPE_F32: torch.float32}
-TOL = {FPK_DTYPE_BF16: 1e-2, FPK_DTYPE_F16: 1e-2, FPK_DTYPE_F32: 5e-3}
+DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16, FPK_DTYPE_F32: torch.float32,
+      FPK_DTYPE_F32_EXACT: torch.float32}
+# FPK_DTYPE_F32_EXACT (the strict-FP32 networks) runs fp32 FMA arithmetic:
+# fp32 rounding of a different summation order only.
+TOL = {FPK_DTYPE_BF16: 1e-2, FPK_DTYPE_F16: 1e-2, FPK_DTYPE_F32: 5e-3, FPK_DTYPE_F32_EXACT: 1e-5}
 
 
 def reference(x: torch.Tensor, layers: int, heads: int, seq: int, n_seq: int) -> torch.Tensor:
@@ -35,7 +38,7 @@ def reference(x: torch.Tensor, layers: int, heads: int, seq: int, n_seq: int) ->
     return torch.cat(outs, 1)
 
 
-@pytest.mark.parametrize("dtype", [FPK_DTYPE_F16, FPK_DTYPE_BF16, FPK_DTYPE_F32])
+@pytest.mark.parametrize("dtype", [FPK_DTYPE_F16, FPK_DTYPE_BF16, FPK_DTYPE_F32, FPK_DTYPE_F32_EXACT])
 @pytest.mark.parametrize("seq,n_seq,layers", [(400, 3, 2), (400, 5, 1), (77, 4, 1), (130, 2, 2)])
 def test_attention_matches_torch(fpk, dtype, seq, n_seq, layers):
     torch.backends.cuda.matmul.allow_tf32 = False

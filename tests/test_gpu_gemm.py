@@ -13,12 +13,13 @@ torch = pytest.importorskip("torch")
 import torch.nn.functional as F  # noqa: E402
 
 from fp_b200.kernels import (FPK_DST_S2D, FPK_DST_SAME, FPK_DST_TOKENS, FPK_DTYPE_BF16,  # noqa: E402
-                             FPK_DTYPE_F16, FPK_DTYPE_F32, GemmDesc, gemm)
+                             FPK_DTYPE_F16, FPK_DTYPE_F32, FPK_DTYPE_F32_EXACT, GemmDesc, gemm)
 from kp8_util import Planar  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16, FPK_DTYPE_F32: torch.float32}
+DT = {FPK_DTYPE_BF16: torch.bfloat16, FPK_DTYPE_F16: torch.float16, FPK_DTYPE_F32: torch.float32,
+      FPK_DTYPE_F32_EXACT: torch.float32}
 
 
 def make_desc(a: Planar, rows, cin, taps_off, w, cout, dst: Planar, dtype, err, bias=None,
@@ -48,7 +49,7 @@ def chunk_major(w_taps: torch.Tensor, dtype=FPK_DTYPE_BF16) -> torch.Tensor:
     """[cout, taps, cin] -> [cout, K'] with k' = chunk*(taps*cw) + tap*cw + c and
     cw = the channels of one 128-byte chunk (64 for 16-bit types, 32 for fp32)."""
     cout, taps, cin = w_taps.shape
-    cw = min(cin, 32 if dtype == FPK_DTYPE_F32 else 64)
+    cw = min(cin, 32 if dtype in (FPK_DTYPE_F32, FPK_DTYPE_F32_EXACT) else 64)
     return (w_taps.reshape(cout, taps, cin // cw, cw).permute(0, 2, 1, 3)
             .reshape(cout, taps * cin).contiguous())
 
@@ -80,6 +81,7 @@ def cta_pairs(request, fpk):
                                               (513, 512, 512, FPK_DTYPE_BF16),
                                               (4096, 512, 1536, FPK_DTYPE_F16),
                                               (777, 128, 128, FPK_DTYPE_F32),
+                                              (777, 128, 256, FPK_DTYPE_F32_EXACT),
                                               (4096, 512, 1536, FPK_DTYPE_F32),
                                               # > 2 x 148 tiles of 128 rows: 256-row tiles with
                                               # one accumulator buffer for 1x1 layers

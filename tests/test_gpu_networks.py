@@ -1,9 +1,10 @@
 """GPU parity of RefineNet / ScoreNet (fpk_net_*, tcgen05 GEMMs + attention)
 against the torch fp32 reference (oracle/fp_net_ref.py) on the same weight
-pack and inputs. Bar: outputs within 1e-2 relative at FP16/BF16 and 1e-3 at
-FP32/TF32 (fp32 activations rounded to nearest TF32 where produced, TF32
-tensor-core multiplies, fp32 accumulation), relative to the output's largest
-magnitude, per output tensor."""
+pack and inputs. Bar: outputs within 1e-2 relative at FP16/BF16, 1e-3 at TF32
+(fp32 activations rounded to nearest TF32 where produced, TF32 tensor-core
+multiplies, fp32 accumulation) and 1e-4 at FP32 (strict: every GEMM the sum of
+three TF32 products of split operands, attention in fp32 FMA arithmetic),
+relative to the output's largest magnitude, per output tensor."""
 from __future__ import annotations
 
 import sys
@@ -23,7 +24,9 @@ from fp_net_ref import NetRef  # noqa: E402
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 FP32, TF32, FP16, BF16 = 0, 1, 2, 3
-TOL = {FP32: 1e-3, TF32: 1e-3, FP16: 1e-2, BF16: 1e-2}
+# FP32 is strict (split-operand GEMMs, fp32 attention): fp32-accurate; TF32
+# runs TF32 products with fp32 accumulation.
+TOL = {FP32: 1e-4, TF32: 1e-3, FP16: 1e-2, BF16: 1e-2}
 
 
 @pytest.fixture(scope="module")
