@@ -46,9 +46,10 @@ PKG = ROOT / "foundation-pose-inference-library_b200"
 sys.path.insert(0, str(PKG / "python"))
 
 N_HYP = 252
-# gemmKernel DRAM traffic per TFLOP of algorithmic GEMM work, from one ncu
-# capture over whole register calls (profiles/gemm_dram_traffic_register.md).
-GEMM_DRAM_BYTES_PER_TFLOP = 28596.3e6 / 28.99
+# GEMM DRAM traffic (read + write) per TFLOP of algorithmic work: ncu captures of
+# three launches each of the three layer classes at 252 images, weighted by
+# their share of a register's FLOPs (profiles/gemm_dram_traffic_layers_b252_fp16.md).
+GEMM_DRAM_BYTES_PER_TFLOP = 1.14e9
 N_ITERS = 5
 W, H = 640, 480
 FP16 = 2
@@ -1131,9 +1132,9 @@ def main() -> None:
                          "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s",
                          "frac": (achieved / pk["bf16"]) if achieved else None, "peak_note": pk["note"],
                          "traffic": GEMM_DRAM_BYTES_PER_TFLOP * (gemm_flops / 1e12) / max(1, gemm_n),
-                         "traffic_note": "DRAM bytes per launch (read + write) from one ncu capture of whole "
-                                         "register calls (profiles/gemm_dram_traffic_register.md), scaled by the "
-                                         "launch's average work",
+                         "traffic_note": "DRAM bytes per launch (read + write): ncu captures of 3 launches of each "
+                                         "GEMM layer class at 252 images, FLOP-weighted, scaled by the launch's "
+                                         "average work (profiles/gemm_dram_traffic_layers_b252_fp16.md)",
                          "launches_timed": gemm_n, "gemm_ms_per_step": gemm_ms / prof_steps,
                          "gemm_tflop_per_step": gemm_flops / prof_steps / 1e12,
                          "measured_on": f"{prof_steps} eager registers (CUDA events per GEMM launch)"},

@@ -116,6 +116,7 @@ struct Plan {
   uint32_t a_slot_bytes;  // CTA-pair kernel: window slot stride (1024-byte aligned)
   uint32_t a_plane_pitch;  // CTA-pair kernel: bytes between channel planes of a window (128-byte aligned)
   int k_splits;            // single-CTA kernel: CTAs sharing one output tile's K range (1 = no split)
+  int withhold_loads;      // failure-injection test: the producer issues no loads (see fpk_gemm_test_withhold_loads)
 };
 
 template <typename T>
@@ -458,7 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t a_iter = 0, b_iter = 0;
       int slot = 0, bs = 0;
       uint32_t a_phase = 0, b_phase = 0;
-      bool ok = true;
+      // A withheld load (failure-injection test) leaves the MMA warp's first
+      // `full` wait to run out: it records error 14 and every role exits.
+      bool ok = pl.withhold_loads == 0;
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
         const int mn = tile / pl.k_splits;
         const int m0 = (mn / pl.n_tiles) * kTileM;
@@ -558,9 +561,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tcCommitElect(&sm->acc_full[buf]);
       }
-      // Drain: wait until every MMA issued above has completed.
+      // Drain: wait until every MMA issued above has completed (also after an
+      // error: TMEM is released only once no MMA can still write it).
       tcCommitElect(&sm->drain);
-      waitBar(&sm->drain, 0, err, 16);
+      drainBar(&sm->drain, 0);
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
@@ -829,7 +833,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tcCommitPairBothElect(&sm->acc_full[buf]);
       }
       tcCommitPairOwnElect(&sm->drain);
-      waitBar(&sm->drain, 0, err, 26);
+      drainBar(&sm->drain, 0);  // as in gemmKernel: no MMA in flight past this point
     }
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
@@ -974,6 +978,7 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
 }
 
 std::atomic<bool> g_cta_pairs{true};
+std::atomic<bool> g_withhold_loads{false};
 template <typename T, int BN, int MH>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
                const CUtensorMap& map_a_tail, size_t smem, cudaStream_t stream) {
@@ -1141,7 +1146,8 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
   const int pair_mh = bn == 256 ? 1 : 2;
   const int pair_planes = pl.cw * esize / 16;
   const int pair_boxes = (pair_mh * kBlockM + (mx - mn) + 127) / 128;  // row-run boxes per window plane
-  if (g_cta_pairs.load() && (bn == 256 || (bn <= 128 && d.cout == bn)) && pair_boxes <= 4 &&
+  const bool withhold = g_withhold_loads.load();
+  if (!withhold && g_cta_pairs.load() && (bn == 256 || (bn <= 128 && d.cout == bn)) && pair_boxes <= 4 &&
       (pair_boxes == 1 || pair_boxes * pair_planes <= 32)) {
     // For 1x1 layers the weight order does not depend on the chunk width
     // (k' = channel), so wider windows (fewer activation barriers per MMA) are
@@ -1238,6 +1244,7 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     while (ks > 1 && static_cast<long long>(tiles) * ks * bn * kBlockM * 4 > d.splitk_ws_bytes) --ks;
     if (ks > 1 && reinterpret_cast<uintptr_t>(d.splitk_ws) % 16 == 0) pl.k_splits = ks;
   }
+  pl.withhold_loads = withhold ? 1 : 0;
   const size_t smem = 1024 + static_cast<size_t>(pl.b_stages) * pl.b_stage_bytes +
                       static_cast<size_t>(pl.a_slots) * pl.a_win_bytes + sizeof(Smem);
   CUtensorMap map;
@@ -1255,4 +1262,8 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
 
 extern "C" int fpk_gemm_set_cta_pairs(int enable) {
   return fpb::gemm::g_cta_pairs.exchange(enable != 0) ? 1 : 0;
+}
+
+extern "C" int fpk_gemm_test_withhold_loads(int enable) {
+  return fpb::gemm::g_withhold_loads.exchange(enable != 0) ? 1 : 0;
 }

@@ -448,6 +448,7 @@ __global__ void convertKernel(const float* __restrict__ in, T* __restrict__ out,
 
 cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, s);
   switch (dtype) {
     case FPK_DTYPE_BF16:
       return launchPdl(layerNorm16Kernel<__nv_bfloat16>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
@@ -464,6 +465,7 @@ cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s) {
 cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int seq_len, int n_seq,
                             float* out, int dtype, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, s);
   switch (dtype) {
     case FPK_DTYPE_BF16:
       return launchPdl(tokenMeanKernel<__nv_bfloat16>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
@@ -478,6 +480,7 @@ cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int
 cudaError_t launchLinearF32(const float* x, const float* w, const float* b, float* y, int m, int n,
                             int k, bool relu, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, s);
   if (n <= 8) {
     return launchPdl(linearFewKernel, dim3((m + 7) / 8), dim3(256), 0, s, x, w, b, y, m, n, k, relu ? 1 : 0);
   }
@@ -487,6 +490,7 @@ cudaError_t launchLinearF32(const float* x, const float* w, const float* b, floa
 
 cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, s);
   return launchPdl(smallAttentionKernel, dim3(len, 4), dim3(128), static_cast<size_t>(len) * sizeof(float), s, qkv, len,
                    out);
 }
@@ -494,6 +498,7 @@ cudaError_t launchSmallAttention(const float* qkv, int len, float* out, cudaStre
 cudaError_t launchNchwToStem(const float* rendered, const float* observed, int n, int H, int W,
                              void* dst, long long plane_stride, int dtype, cudaStream_t s) {
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, s);
   const long long total = 2LL * n * H * W;
   const unsigned grid = static_cast<unsigned>((total + 255) / 256);
   auto* d = static_cast<unsigned char*>(dst);

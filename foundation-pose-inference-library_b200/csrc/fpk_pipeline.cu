@@ -1217,6 +1217,7 @@ int fpk_crop_boxes(const float* poses, int n, fpk_intrinsics_t k, float diameter
   if (validateParams(p) != 0) return 1;
   if (n <= 0) return fail("fpk_crop_boxes: n must be positive");
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, static_cast<cudaStream_t>(stream));
   cropBoxesKernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       poses, n, k, diameter, p->crop_ratio, reinterpret_cast<float4*>(boxes));
   return checkLaunch("cropBoxesKernel");
@@ -1325,6 +1326,7 @@ int fpk_apply_deltas(float* poses, const float* delta_t, const float* delta_r, i
   if (validateParams(p) != 0) return 1;
   if (n <= 0) return fail("fpk_apply_deltas: n must be positive");
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, static_cast<cudaStream_t>(stream));
   applyDeltasKernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       poses, delta_t, delta_r, n, diameter, p->rotation_normalizer_rad);
   return checkLaunch("applyDeltasKernel");
@@ -1334,6 +1336,7 @@ int fpk_select_best(const float* poses, const float* scores, int n, const float*
                     float* result, void* stream) {
   if (n <= 0 || center3 == nullptr) return fail("fpk_select_best: bad arguments");
   prof::countLaunch(prof::kOther);
+  prof::Scope scope(prof::kOther, 0.0, static_cast<cudaStream_t>(stream));
   selectBestKernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       poses, scores, n, center3[0], center3[1], center3[2], result);
   return checkLaunch("selectBestKernel");

@@ -243,6 +243,15 @@ FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
  * returns the previous setting. No reference counterpart (a tuning switch). */
 FP_API int fpk_gemm_set_cta_pairs(int enable);
 
+/* Failure-injection test switch (no reference counterpart). With enable != 0
+ * every following fpk_gemm runs on single-CTA tiles whose producer issues no
+ * loads, so the MMA warp's bounded wait for its first operand tile runs out
+ * (~2 s): the kernel records a non-zero code in desc->error_flag, every role
+ * exits without leaving a copy or an MMA in flight, and the context stays
+ * usable. The output is not written. Process-wide; returns the previous
+ * setting. Used by the tests of the bounded-wait error path only. */
+FP_API int fpk_gemm_test_withhold_loads(int enable);
+
 /* Fused multi-head self-attention on tcgen05/TMEM (head dim 128):
  * out = softmax(Q K^T / sqrt(128)) V for every (layer, head, sequence), over
  * planar activations of `dtype` (fp16/bf16 KP8, or fp32 KP4 run as TF32).

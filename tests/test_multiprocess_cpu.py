@@ -115,3 +115,49 @@ def test_gather_shards_assembles_hypothesis_order(n, world):
     for _, order, rows_ok in res:
         assert order == [float(i) for i in range(n)]  # every rank, same order, no padding
         assert rows_ok
+
+
+def _failing_rank_worker(rank, world, port, q):
+    """Rank 1 fails between steps (an exception before its shard's gather, as
+    a failed fp_register_shard_begin would raise) and leaves; rank 0 must get
+    an error from its gather within the process group's short timeout
+    instead of waiting for good."""
+    import sys
+    import time
+    from datetime import timedelta
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "foundation-pose-inference-library_b200" / "python"))
+    from fp_b200.sharded import gather_shards
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    n = 8
+    local = torch.zeros((-(-n // world), 4))
+    gather_shards(local, n)  # one good step on every rank
+    if rank == 1:
+        q.put((rank, "raised"))
+        raise SystemExit(3)  # the failing rank leaves without joining the next gather
+    t0 = time.monotonic()
+    try:
+        gather_shards(local, n)
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - any collective error is the expected outcome
+        q.put((rank, f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}"))
+
+
+def test_failed_rank_ends_peer_gather_with_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode is not None for p in procs)  # nobody hangs
+    assert procs[1].exitcode == 3
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert res[1] == "raised"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2]) < 60.0
