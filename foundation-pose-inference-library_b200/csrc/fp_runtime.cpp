@@ -406,8 +406,23 @@ struct FoundationPose::Impl {
   cudaGraphExec_t graph_exec = nullptr;
   int graph_batch = 0, graph_w = 0, graph_h = 0;
   CameraIntrinsics graph_k{};
+  // Whole track call (preprocess -> previous pose -> passes -> select) as one
+  // graph, kept apart from the register's refinement graph so alternating
+  // register and track calls re-capture neither.
+  cudaGraphExec_t track_exec = nullptr;
+  int track_iters = -1, track_w = 0, track_h = 0;
+  CameraIntrinsics track_k{};
 
-  ~Impl() { destroyGraph(); }
+  ~Impl() {
+    destroyGraph();
+    destroyTrackGraph();
+  }
+
+  void destroyTrackGraph() noexcept {
+    if (track_exec != nullptr) cudaGraphExecDestroy(track_exec);
+    track_exec = nullptr;
+    track_iters = -1;
+  }
 
   void destroyGraph() noexcept {
     if (graph_exec != nullptr) cudaGraphExecDestroy(graph_exec);
@@ -522,6 +537,54 @@ struct FoundationPose::Impl {
     graph_w = w;
     graph_h = h;
     graph_k = k;
+  }
+
+  // Device work of one track call after the frame upload (reference
+  // src/foundation_pose.cpp:379-410).
+  void trackBody(int iters, int w, int h, CameraIntrinsics k) {
+    fpkCheck(fpk_preprocess(depth_raw.as<float>(), nullptr, w, h, toK(k), &params, depth_filtered.as<float>(),
+                            nullptr, nullptr, nullptr, s()));
+    checkCuda(cudaMemcpyAsync(poses.data(), prev_pose.data(), 64, cudaMemcpyDeviceToDevice, s()),
+              "cudaMemcpyAsync device pose");
+    for (int i = 0; i < iters; ++i) refinePass(1, 1, w, h, k);
+    const float center[3] = {mesh.center.x, mesh.center.y, mesh.center.z};
+    fpkCheck(fpk_select_best(poses.as<float>(), one.as<float>(), 1, center, best.as<float>(), s()));
+    checkCuda(cudaMemcpyAsync(prev_pose.data(), poses.data(), 64, cudaMemcpyDeviceToDevice, s()),
+              "cudaMemcpyAsync device pose");
+  }
+
+  void trackCall(int iters, int w, int h, CameraIntrinsics k) {
+    if (!cfg.capture_cuda_graph) {
+      trackBody(iters, w, h, k);
+      return;
+    }
+    const bool stale = track_exec == nullptr || track_iters != iters || track_w != w || track_h != h ||
+                       track_k.fx != k.fx || track_k.fy != k.fy || track_k.cx != k.cx || track_k.cy != k.cy;
+    if (stale) {
+      destroyTrackGraph();
+      inference->prepareForBatch(1);
+      checkCuda(cudaStreamBeginCapture(s(), cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+      cudaGraph_t g = nullptr;
+      try {
+        trackBody(iters, w, h, k);
+      } catch (...) {
+        cudaStreamEndCapture(s(), &g);
+        if (g != nullptr) cudaGraphDestroy(g);
+        throw;
+      }
+      checkCuda(cudaStreamEndCapture(s(), &g), "cudaStreamEndCapture");
+      const cudaError_t e = cudaGraphInstantiate(&track_exec, g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) {
+        track_exec = nullptr;
+        checkCuda(e, "cudaGraphInstantiate track graph");
+      }
+      track_iters = iters;
+      track_w = w;
+      track_h = h;
+      track_k = k;
+    }
+    checkCuda(cudaGraphLaunch(track_exec, s()), "cudaGraphLaunch track graph");
   }
 
   void checkNetworkErrors() {
@@ -793,15 +856,7 @@ PoseEstimate FoundationPose::trackFrame(const std::uint8_t* rgb_u8, const float*
   if (!I.has_prev) throw FoundationPoseError("No previous pose. Call registerFrame before trackFrame.");
   const int iters = n_refine >= 0 ? n_refine : I.cfg.n_track_iters;
   I.upload(rgb_u8, depth_m, nullptr, width, height);
-  fpkCheck(fpk_preprocess(I.depth_raw.as<float>(), nullptr, width, height, toK(intrinsics), &I.params,
-                          I.depth_filtered.as<float>(), nullptr, nullptr, nullptr, I.s()));
-  checkCuda(cudaMemcpyAsync(I.poses.data(), I.prev_pose.data(), 64, cudaMemcpyDeviceToDevice, I.s()),
-            "cudaMemcpyAsync device pose");
-  I.refinementLoop(iters, 1, 1, width, height, intrinsics);
-  const float center[3] = {I.mesh.center.x, I.mesh.center.y, I.mesh.center.z};
-  fpkCheck(fpk_select_best(I.poses.as<float>(), I.one.as<float>(), 1, center, I.best.as<float>(), I.s()));
-  checkCuda(cudaMemcpyAsync(I.prev_pose.data(), I.poses.data(), 64, cudaMemcpyDeviceToDevice, I.s()),
-            "cudaMemcpyAsync device pose");
+  I.trackCall(iters, width, height, intrinsics);
   return I.readBest();
 }
 

@@ -155,6 +155,30 @@ def test_cuda_graph_register_matches_eager(env):
     lib.destroy(h2)
 
 
+def test_cuda_graph_track_matches_eager(env):
+    """With capture_cuda_graph the whole track call after the upload replays as
+    one graph (and the register keeps its own refinement graph): poses equal
+    the eager path's bit for bit, across alternating register and track calls,
+    different iteration counts and host or device frames."""
+    lib, scene = env["lib"], env["scene"]
+    h1, _ = create(env, n_hyp=42)
+    h2, _ = create(env, n_hyp=42, graph=True)
+    seq = [("register", 2, False), ("track", 2, False), ("track", 2, True), ("track", 3, False),
+           ("register", 2, True), ("track", 2, False), ("track", 2, False)]
+    for kind, iters, dev in seq:
+        out = []
+        for h in (h1, h2):
+            if kind == "register":
+                out.append(register(lib, h, view(scene, device=dev), n_refine=iters))
+            else:
+                out.append(track(lib, h, view(scene, device=dev, mask=False), n_refine=iters))
+        (rc1, p1, s1, e1), (rc2, p2, s2, e2) = out
+        assert rc1 == 0 and rc2 == 0, (kind, e1, e2)
+        assert np.array_equal(p1, p2) and s1 == s2, (kind, iters)
+    lib.destroy(h1)
+    lib.destroy(h2)
+
+
 def test_group_matches_single_and_skips(env):
     lib, scene = env["lib"], env["scene"]
     g = lib.group_create([options(env), options(env)], config(env, n_hyp=42))
