@@ -216,6 +216,11 @@ __global__ void __launch_bounds__(256, 2) layerNorm16Kernel(LnArgs a) {
 }
 
 // Mean over the seq_len rows of each sequence, 512 channels, fp32 out.
+// Grid (sequences, plane groups of 8): warp w of a block owns channel plane
+// 8 * blockIdx.y + w; lane l adds rows l, l + 32, ... (four rows' records in
+// flight per lane, 512 contiguous bytes per warp-wide load), then a butterfly
+// over the 32 lanes. A sequence's mean no longer waits on one CTA's serial
+// walk over its 400 rows (the one-hypothesis passes of tracking).
 template <typename T>
 __global__ void __launch_bounds__(256) tokenMeanKernel(const unsigned char* __restrict__ in,
                                                        long long plane_stride, int seq_len,
@@ -223,60 +228,61 @@ __global__ void __launch_bounds__(256) tokenMeanKernel(const unsigned char* __re
   tc::pdlTrigger();
   tc::pdlWait();
   constexpr int kPR = 16 / static_cast<int>(sizeof(T));
-  constexpr int kPlanes = 512 / kPR;
-  constexpr int kSubs = 256 / kPlanes;  // row interleave per plane: 4 (16-bit) or 2 (fp32)
-  __shared__ float part[kSubs][512];
-  const int plane = threadIdx.x / kSubs;
-  const int sub = threadIdx.x % kSubs;
+  const int lane = threadIdx.x & 31;
+  const int plane = blockIdx.y * 8 + (threadIdx.x >> 5);
   const long long base = static_cast<long long>(blockIdx.x) * seq_len;
-  float acc[kPR] = {};
   const unsigned char* src = in + static_cast<long long>(plane) * plane_stride + base * 16;
-  // Four rows' records are requested before any is added (the sum keeps the
-  // row order r, r + kSubs, ...), so each thread has four loads in flight.
-  int r = sub;
-  for (; r + 3 * kSubs < seq_len; r += 4 * kSubs) {
+  float acc[kPR] = {};
+  int r = lane;
+  for (; r + 96 < seq_len; r += 128) {
     alignas(16) T rec[4][kPR];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      *reinterpret_cast<uint4*>(rec[u]) = *reinterpret_cast<const uint4*>(src + static_cast<long long>(r + u * kSubs) * 16);
+      *reinterpret_cast<uint4*>(rec[u]) = *reinterpret_cast<const uint4*>(src + static_cast<long long>(r + 32 * u) * 16);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
 #pragma unroll
-      for (int i = 0; i < kPR; ++i) acc[i] += toF<T>(rec[u][i]);
+      for (int e = 0; e < kPR; ++e) acc[e] += toF<T>(rec[u][e]);
     }
   }
-  for (; r < seq_len; r += kSubs) {
+  for (; r < seq_len; r += 32) {
     alignas(16) T rec[kPR];
     *reinterpret_cast<uint4*>(rec) = *reinterpret_cast<const uint4*>(src + static_cast<long long>(r) * 16);
 #pragma unroll
-    for (int i = 0; i < kPR; ++i) acc[i] += toF<T>(rec[i]);
+    for (int e = 0; e < kPR; ++e) acc[e] += toF<T>(rec[e]);
   }
 #pragma unroll
-  for (int e = 0; e < kPR; ++e) part[sub][plane * kPR + e] = acc[e];
-  __syncthreads();
-  for (int c = threadIdx.x; c < 512; c += 256) {
-    float t = part[0][c];
+  for (int off = 16; off > 0; off >>= 1) {
 #pragma unroll
-    for (int q = 1; q < kSubs; ++q) t += part[q][c];
-    out[blockIdx.x * 512 + c] = t / seq_len;
+    for (int e = 0; e < kPR; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], off);
+  }
+  if (lane < kPR) {
+    float v = acc[0];
+#pragma unroll
+    for (int e = 1; e < kPR; ++e) v = lane == e ? acc[e] : v;
+    out[blockIdx.x * 512 + plane * kPR + lane] = v / seq_len;
   }
 }
 
 // y[m][n] = sum_k x[m][k] * w[n][k] + b[n] (+ relu) for n <= 8 outputs (the
-// 512 -> 3 pose heads and the 512 -> 1 score head): one warp per row, lane j
-// takes k = j, j + 32, ... (coalesced row reads), then a butterfly per output.
+// 512 -> 3 pose heads and the 512 -> 1 score head): one block per row, thread
+// t takes k = t, t + 256, ... (coalesced row reads, every load of a thread
+// issued before its products), then a butterfly per warp and the 8 warps'
+// sums added in warp order.
 __global__ void __launch_bounds__(256) linearFewKernel(const float* __restrict__ x, const float* __restrict__ w,
                                                        const float* __restrict__ b, float* __restrict__ y, int m,
                                                        int n, int k, int relu) {
   tc::pdlTrigger();
   tc::pdlWait();
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  __shared__ float part[8][8];
+  const int row = blockIdx.x;
   const int lane = threadIdx.x & 31;
-  if (row >= m) return;
+  const int warp = threadIdx.x >> 5;
   float acc[8] = {};
   const float* xr = x + static_cast<long long>(row) * k;
-  for (int kk = lane; kk < k; kk += 32) {
+#pragma unroll 4
+  for (int kk = threadIdx.x; kk < k; kk += 256) {
     const float xv = xr[kk];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -288,12 +294,17 @@ __global__ void __launch_bounds__(256) linearFewKernel(const float* __restrict__
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
   }
-  if (lane < n) {
-    float v = 0.0f;
+  if (lane == 0) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v = lane == j ? acc[j] : v;
-    v += b != nullptr ? b[lane] : 0.0f;
-    y[static_cast<long long>(row) * n + lane] = relu ? fmaxf(v, 0.0f) : v;
+    for (int j = 0; j < 8; ++j) part[warp][j] = acc[j];
+  }
+  __syncthreads();
+  if (threadIdx.x < n) {
+    float v = part[0][threadIdx.x];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) v += part[q][threadIdx.x];
+    v += b != nullptr ? b[threadIdx.x] : 0.0f;
+    y[static_cast<long long>(row) * n + threadIdx.x] = relu ? fmaxf(v, 0.0f) : v;
   }
 }
 
@@ -468,12 +479,12 @@ cudaError_t launchTokenMean(const unsigned char* in, long long plane_stride, int
   prof::Scope scope(prof::kOther, 0.0, s);
   switch (dtype) {
     case FPK_DTYPE_BF16:
-      return launchPdl(tokenMeanKernel<__nv_bfloat16>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
+      return launchPdl(tokenMeanKernel<__nv_bfloat16>, dim3(n_seq, 64 / 8), dim3(256), 0, s, in, plane_stride, seq_len, out);
     case FPK_DTYPE_F32:
     case FPK_DTYPE_F32_EXACT:
-      return launchPdl(tokenMeanKernel<float>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
+      return launchPdl(tokenMeanKernel<float>, dim3(n_seq, 128 / 8), dim3(256), 0, s, in, plane_stride, seq_len, out);
     default:
-      return launchPdl(tokenMeanKernel<__half>, dim3(n_seq), dim3(256), 0, s, in, plane_stride, seq_len, out);
+      return launchPdl(tokenMeanKernel<__half>, dim3(n_seq, 64 / 8), dim3(256), 0, s, in, plane_stride, seq_len, out);
   }
 }
 
@@ -482,7 +493,7 @@ cudaError_t launchLinearF32(const float* x, const float* w, const float* b, floa
   prof::countLaunch(prof::kOther);
   prof::Scope scope(prof::kOther, 0.0, s);
   if (n <= 8) {
-    return launchPdl(linearFewKernel, dim3((m + 7) / 8), dim3(256), 0, s, x, w, b, y, m, n, k, relu ? 1 : 0);
+    return launchPdl(linearFewKernel, dim3(m), dim3(256), 0, s, x, w, b, y, m, n, k, relu ? 1 : 0);
   }
   const dim3 grid((n + 31) / 32, (m + 31) / 32);
   return launchPdl(linearF32Kernel, grid, dim3(256), 0, s, x, w, b, y, m, n, k, relu ? 1 : 0);
