@@ -172,8 +172,11 @@ std::vector<float> s2dTaps(const std::vector<float>& w, int cout, int cin, int k
 
 class Network {
  public:
-  Network(const WeightPack& pack, int dtype, std::vector<void*>& allocs)
-      : dtype_(dtype), allocs_(allocs), arch_(pack.arch) {
+  // Uploads go through `setup`, a private non-blocking stream: no legacy-stream
+  // work and no device-wide synchronisation, so a network can be built while
+  // another thread captures a CUDA graph on the same device (group objects).
+  Network(const WeightPack& pack, int dtype, std::vector<void*>& allocs, cudaStream_t setup)
+      : dtype_(dtype), allocs_(allocs), arch_(pack.arch), setup_(setup) {
     // Encoder.
     conv("encA.conv1", pack, s2dTaps(pack.at("encA.conv1.w"), 64, 6, 7, 8), 64, 32, 16, offsets(4, kStemGrid),
          2.0 * 64 * 49 * 6);
@@ -224,7 +227,7 @@ class Network {
         f32[n] = upload(pack.at(n));
       }
     }
-    check(cudaDeviceSynchronize(), "weight upload");
+    check(cudaStreamSynchronize(setup_), "weight upload");
   }
 
   const ConvLayer& L(const std::string& n) const {
@@ -251,7 +254,8 @@ class Network {
     void* p = nullptr;
     check(cudaMalloc(&p, v.size() * 4 + 16), "cudaMalloc weights");
     allocs_.push_back(p);
-    check(cudaMemcpy(p, v.data(), v.size() * 4, cudaMemcpyHostToDevice), "upload weights");
+    // From pageable memory the call returns once `v` has been staged.
+    check(cudaMemcpyAsync(p, v.data(), v.size() * 4, cudaMemcpyHostToDevice, setup_), "upload weights");
     return static_cast<float*>(p);
   }
 
@@ -268,15 +272,14 @@ class Network {
   void* uploadWeights(const std::vector<float>& v) {
     if (dtype_ == FPK_DTYPE_F32 || dtype_ == FPK_DTYPE_F32_EXACT) return upload(roundTf32(v));
     float* tmp = nullptr;
-    check(cudaMalloc(&tmp, v.size() * 4), "cudaMalloc staging");
-    check(cudaMemcpy(tmp, v.data(), v.size() * 4, cudaMemcpyHostToDevice), "upload staging");
+    check(cudaMallocAsync(reinterpret_cast<void**>(&tmp), v.size() * 4, setup_), "cudaMallocAsync staging");
+    check(cudaMemcpyAsync(tmp, v.data(), v.size() * 4, cudaMemcpyHostToDevice, setup_), "upload staging");
     void* p = nullptr;
     check(cudaMalloc(&p, v.size() * 2 + 16), "cudaMalloc weights");
     allocs_.push_back(p);
-    check(net::launchConvert(tmp, p, static_cast<long long>(v.size()), dtype_ == FPK_DTYPE_BF16, nullptr),
+    check(net::launchConvert(tmp, p, static_cast<long long>(v.size()), dtype_ == FPK_DTYPE_BF16, setup_),
           "convert weights");
-    check(cudaDeviceSynchronize(), "convert weights");
-    cudaFree(tmp);
+    check(cudaFreeAsync(tmp, setup_), "cudaFreeAsync staging");
     return p;
   }
 
@@ -320,6 +323,7 @@ class Network {
   int dtype_;
   std::vector<void*>& allocs_;
   int arch_;
+  cudaStream_t setup_;
 };
 
 // ---------------------------------------------------------------------------
@@ -338,7 +342,7 @@ namespace {
 
 // Planar buffer of `channels` channels, `per_record` channels per 16-byte
 // record (8 for fp16/bf16, 4 for fp32).
-Planar allocPlanar(std::vector<void*>& allocs, long long rows, int channels, int per_record) {
+Planar allocPlanar(std::vector<void*>& allocs, long long rows, int channels, int per_record, cudaStream_t setup) {
   Planar p;
   p.rows = rows;
   p.planes = channels / per_record;
@@ -346,7 +350,7 @@ Planar allocPlanar(std::vector<void*>& allocs, long long rows, int channels, int
   p.bytes = static_cast<size_t>(p.plane_stride) * p.planes;
   check(cudaMalloc(&p.mem, p.bytes), "cudaMalloc activations");
   allocs.push_back(p.mem);
-  check(cudaMemset(p.mem, 0, p.bytes), "zero activations");
+  check(cudaMemsetAsync(p.mem, 0, p.bytes, setup), "zero activations");
   p.base = static_cast<unsigned char*>(p.mem) + kGuardPre * 16;
   return p;
 }
@@ -369,31 +373,33 @@ NetworkRunner::NetworkRunner(const std::string& refine_path, const std::string& 
   if (max_batch <= 0 || max_batch > 1024) throw std::runtime_error("max batch must be in [1, 1024]");
   const int dt = dtype();
   const int pr = perRecord();
+  cudaStream_t setup = nullptr;
+  check(cudaStreamCreateWithFlags(&setup, cudaStreamNonBlocking), "set-up stream");
   try {
     WeightPack rp = WeightPack::load(refine_path);
     WeightPack sp = WeightPack::load(score_path);
     if (rp.arch != 0) throw std::runtime_error(refine_path + " is not a RefineNet pack");
     if (sp.arch != 1) throw std::runtime_error(score_path + " is not a ScoreNet pack");
-    refine_ = std::make_unique<Network>(rp, dt, allocations_);
-    score_ = std::make_unique<Network>(sp, dt, allocations_);
+    refine_ = std::make_unique<Network>(rp, dt, allocations_, setup);
+    score_ = std::make_unique<Network>(sp, dt, allocations_, setup);
     const long long B = max_batch;
     const long long N = 2 * B;
-    stem_ = allocPlanar(allocations_, N * kStemGrid * kStemGrid, 32, pr);
+    stem_ = allocPlanar(allocations_, N * kStemGrid * kStemGrid, 32, pr, setup);
     act_ = std::make_unique<Act>();
     Act& a = *act_;
-    a.x1 = allocPlanar(allocations_, N * kG40 * kG40, 256, pr);
-    for (auto& p : a.e) p = allocPlanar(allocations_, N * kG40 * kG40, 128, pr);
-    for (auto& p : a.ab) p = allocPlanar(allocations_, B * kG40 * kG40, 256, pr);
-    a.x4 = allocPlanar(allocations_, B * kG20 * kG20, 1024, pr);
-    for (auto& p : a.f) p = allocPlanar(allocations_, B * kG20 * kG20, 512, pr);
+    a.x1 = allocPlanar(allocations_, N * kG40 * kG40, 256, pr, setup);
+    for (auto& p : a.e) p = allocPlanar(allocations_, N * kG40 * kG40, 128, pr, setup);
+    for (auto& p : a.ab) p = allocPlanar(allocations_, B * kG40 * kG40, 256, pr, setup);
+    a.x4 = allocPlanar(allocations_, B * kG20 * kG20, 1024, pr, setup);
+    for (auto& p : a.f) p = allocPlanar(allocations_, B * kG20 * kG20, 512, pr, setup);
     const long long T = B * kTokens;
-    a.tok = allocPlanar(allocations_, T, kEmbed, pr);
-    a.qkv = allocPlanar(allocations_, T, 6 * kEmbed, pr);
-    a.att = allocPlanar(allocations_, T, 2 * kEmbed, pr);
-    a.y1 = allocPlanar(allocations_, T, kEmbed, pr);
-    a.x1n = allocPlanar(allocations_, T, kEmbed, pr);
-    a.h = allocPlanar(allocations_, T, kEmbed, pr);
-    a.y2 = allocPlanar(allocations_, T, kEmbed, pr);
+    a.tok = allocPlanar(allocations_, T, kEmbed, pr, setup);
+    a.qkv = allocPlanar(allocations_, T, 6 * kEmbed, pr, setup);
+    a.att = allocPlanar(allocations_, T, 2 * kEmbed, pr, setup);
+    a.y1 = allocPlanar(allocations_, T, kEmbed, pr, setup);
+    a.x1n = allocPlanar(allocations_, T, kEmbed, pr, setup);
+    a.h = allocPlanar(allocations_, T, kEmbed, pr, setup);
+    a.y2 = allocPlanar(allocations_, T, kEmbed, pr, setup);
     a.feat = allocF32(allocations_, 2 * B * kEmbed);
     a.qkvc = allocF32(allocations_, B * 3 * kEmbed);
     a.oc = allocF32(allocations_, B * kEmbed);
@@ -401,7 +407,7 @@ NetworkRunner::NetworkRunner(const std::string& refine_path, const std::string& 
     void* e = nullptr;
     check(cudaMalloc(&e, 16), "cudaMalloc error flag");
     allocations_.push_back(e);
-    check(cudaMemset(e, 0, 16), "zero error flag");
+    check(cudaMemsetAsync(e, 0, 16, setup), "zero error flag");
     err_ = static_cast<int*>(e);
     if (dt == FPK_DTYPE_F32_EXACT) {
       // Largest split activation (a GEMM input: x1, 2B images x 41^2 rows x
@@ -423,7 +429,11 @@ NetworkRunner::NetworkRunner(const std::string& refine_path, const std::string& 
     splitk_bytes_ = 24ll << 20;
     check(cudaMalloc(&splitk_, static_cast<size_t>(splitk_bytes_)), "cudaMalloc split-K scratch");
     allocations_.push_back(splitk_);
+    check(cudaStreamSynchronize(setup), "network set-up");
+    cudaStreamDestroy(setup);
   } catch (...) {
+    cudaStreamSynchronize(setup);
+    cudaStreamDestroy(setup);
     for (void* p : allocations_) cudaFree(p);
     allocations_.clear();
     throw;
