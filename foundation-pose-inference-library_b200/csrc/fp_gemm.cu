@@ -61,6 +61,7 @@ constexpr int kMaxASlots = 8;
 constexpr int kMaxBStages = 16;
 constexpr int kMaxStagesPerChunk = FPK_GEMM_MAX_TAPS;  // 64-channel chunks: one stage per tap
 constexpr size_t kSmemBytes = 220 * 1024;  // dynamic shared memory per CTA
+constexpr size_t kOutStageBytes = 8 * 2 * 2048;  // staged output chunks: 8 epilogue warps x 2 x [4 planes][32 rows][16 B]
 
 struct Smem {
   uint64_t a_full[kMaxASlots], a_empty[kMaxASlots];
@@ -117,6 +118,8 @@ struct Plan {
   uint32_t a_plane_pitch;  // CTA-pair kernel: bytes between channel planes of a window (128-byte aligned)
   int k_splits;            // single-CTA kernel: CTAs sharing one output tile's K range (1 = no split)
   int withhold_loads;      // failure-injection test: the producer issues no loads (see fpk_gemm_test_withhold_loads)
+  int tma_store;           // CTA-pair kernel, dense 16-bit outputs: epilogue stages 32-column chunks, TMA stores them
+  uint32_t stage_off;      // offset of the staging area (8 warps x 2 x 2 KB) from the aligned dynamic smem base
 };
 
 template <typename T>
@@ -254,8 +257,8 @@ __device__ __forceinline__ RowDst rowDst(const fpk_gemm_desc_t& d, int r) {
 // Bias / residual / ReLU / positional embedding on the accumulator values of
 // output channels n..n+7 of one row, stored into the destination layout.
 template <typename T>
-__device__ __forceinline__ void finish8(const fpk_gemm_desc_t& d, const RowDst& rd, float* v, int n,
-                                        const uint4* res_rec, bool has_res) {
+__device__ __forceinline__ void apply8(const fpk_gemm_desc_t& d, const RowDst& rd, float* v, int n,
+                                       const uint4* res_rec, bool has_res) {
   if (d.bias != nullptr) {
     const float4 b0 = __ldg(reinterpret_cast<const float4*>(d.bias + n));
     const float4 b1 = __ldg(reinterpret_cast<const float4*>(d.bias + n + 4));
@@ -277,6 +280,12 @@ __device__ __forceinline__ void finish8(const fpk_gemm_desc_t& d, const RowDst& 
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] += __ldg(pp + e);
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void finish8(const fpk_gemm_desc_t& d, const RowDst& rd, float* v, int n,
+                                        const uint4* res_rec, bool has_res) {
+  apply8<T>(d, rd, v, n, res_rec, has_res);
   storeRec8<T>(static_cast<unsigned char*>(d.dst), d.dst_plane_stride, rd.ch_base + n, rd.drow, v,
                d.dtype == FPK_DTYPE_F32_EXACT);
 }
@@ -365,6 +374,65 @@ __device__ __forceinline__ void epilogueRow(const fpk_gemm_desc_t& d, uint32_t t
         finish8<T>(d, rd, v, n0 + j + g * 8, rv[g], has_res);
       }
     }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      rv[g][0] = rn[g][0];
+      rv[g][1] = rn[g][1];
+    }
+  }
+}
+
+// Staged epilogue of a dense 16-bit layer (SAME layout, every row valid):
+// like epilogueRow, but each 32-column chunk of the warp's 32 rows is packed
+// into a 2 KB shared-memory tile ([4 planes][32 rows][16 B], two per warp,
+// alternating) and written by one bulk tensor store issued by lane 0, instead
+// of 16-byte stores from every thread (which set the pace of short-K layers).
+// r0 = the warp's first output row (a multiple of 32); rows past the layer's
+// end are clipped by the tensor map. `chunks` counts this warp's chunks so far.
+template <typename T, int kSpan>
+__device__ __forceinline__ void epilogueRowStaged(const fpk_gemm_desc_t& d, uint32_t t_base, int r, int n0, int j0,
+                                                  unsigned char* stage, const CUtensorMap* tmap_out, int r0,
+                                                  uint32_t& chunks) {
+  static_assert(Elem<T>::kPerRecord == 8, "16-bit outputs only");
+  const int lane = threadIdx.x & 31;
+  const unsigned char* res = static_cast<const unsigned char*>(d.residual);
+  const RowDst rd = rowDst(d, r);
+  const bool has_res = rd.valid && res != nullptr;
+  uint4 rv[4][2] = {}, rn[4][2] = {};
+  if (has_res) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j0 + g * 8, r, rv[g]);
+  }
+#pragma unroll 1
+  for (int j = j0; j < j0 + kSpan; j += 32) {
+    uint32_t acc[32];
+    FPB_TMEM_LD32(t_base + j, acc);
+    if (has_res && j + 32 < j0 + kSpan) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) loadRec8<T>(res, d.res_plane_stride, n0 + j + 32 + g * 8, r, rn[g]);
+    }
+    unsigned char* sb = stage + (chunks & 1u) * 2048u;
+    if (chunks >= 2) {
+      // The store issued two chunks ago from this buffer has read it.
+      if (lane == 0) bulkWaitRead<1>();
+      __syncwarp();
+    }
+    tmemWaitLd();
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[g * 8 + e]);
+      apply8<T>(d, rd, v, n0 + j + g * 8, rv[g], has_res);
+      *reinterpret_cast<uint4*>(sb + g * 512 + lane * 16) = pack8<T>(v);
+    }
+    fenceProxyAsyncSmem();
+    __syncwarp();
+    if (lane == 0) {
+      tmaStore2d(tmap_out, 2 * r0, (n0 + j) / 8, sb);
+      bulkCommit();
+    }
+    ++chunks;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       rv[g][0] = rn[g][0];
@@ -642,7 +710,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T, int BN, int MH>
 __global__ void __launch_bounds__(kThreads, 1)
     gemmPairKernel(const fpk_gemm_desc_t d, const Plan pl, const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_tail) {
+                   const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a_tail,
+                   const __grid_constant__ CUtensorMap tmap_out) {
   pdlTrigger();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -842,6 +911,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kSpan = MH == 1 ? BN / 2 : BN;  // columns converted by one warp
     const int m_half = MH == 1 ? 0 : pair;
     const int row_in_tile = static_cast<int>(rank) * kCtaM + m_half * kBlockM + quarter * 32 + lane;
+    unsigned char* stage = base + pl.stage_off + static_cast<size_t>(warp - 2) * 4096;
+    uint32_t chunks = 0;
     uint32_t t_iter = 0;
     for (int tile = pair_id; tile < n_tiles_total; tile += n_pairs, ++t_iter) {
       const int m0 = (tile / pl.n_tiles) * kPairM;
@@ -851,11 +922,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       tcFenceAfter();
       const uint32_t t_base =
           tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>((buf * MH + m_half) * BN);
-      epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, MH == 1 ? pair * kSpan : 0);
+      bool staged = false;
+      if constexpr (!Elem<T>::kTf32) {
+        if (pl.tma_store) {
+          epilogueRowStaged<T, kSpan>(d, t_base, m0 + row_in_tile, n0, MH == 1 ? pair * kSpan : 0, stage, &tmap_out,
+                                      m0 + row_in_tile - lane, chunks);
+          staged = true;
+        }
+      }
+      if (!staged) epilogueRow<T, kSpan>(d, t_base, m0 + row_in_tile, n0, MH == 1 ? pair * kSpan : 0);
       tcFenceBefore();
       __syncwarp();
       if (lane == 0) mbarArriveCluster(mapaShared(smemU32(&sm->acc_empty[buf]), 0));
     }
+    // Every bulk store this warp issued has completed before the CTA exits.
+    if (lane == 0 && chunks > 0) bulkWaitAll();
+    __syncwarp();
   }
   __syncthreads();
   tcFenceBefore();
@@ -920,10 +1002,10 @@ int makeWeightMap(const fpk_gemm_desc_t& d, int kprime, int bn, CUtensorMap* map
 // stage per window) with as many slots as stages. Returns false if fewer than
 // two of each fit.
 bool chooseSlots(uint32_t slot_bytes, uint32_t stage_bytes, int stages_per_chunk, int* slots_out,
-                 int* stages_out) {
+                 int* stages_out, size_t reserve = 0) {
   int best = -1;
   for (int slots = 2; slots <= kMaxASlots; ++slots) {
-    const size_t used = 1024 + sizeof(Smem) + static_cast<size_t>(slots) * slot_bytes;
+    const size_t used = 1024 + sizeof(Smem) + reserve + static_cast<size_t>(slots) * slot_bytes;
     if (used >= kSmemBytes) break;
     int stages = static_cast<int>((kSmemBytes - used) / stage_bytes);
     stages = stages > kMaxBStages ? kMaxBStages : stages;
@@ -979,9 +1061,10 @@ int launch(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map, siz
 
 std::atomic<bool> g_cta_pairs{true};
 std::atomic<bool> g_withhold_loads{false};
+std::atomic<bool> g_tma_store{true};
 template <typename T, int BN, int MH>
 int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_w, const CUtensorMap& map_a,
-               const CUtensorMap& map_a_tail, size_t smem, cudaStream_t stream) {
+               const CUtensorMap& map_a_tail, const CUtensorMap& map_out, size_t smem, cudaStream_t stream) {
   static DeviceOnce smem_attr;
   static std::mutex mu;
   static std::unordered_map<long long, int> clusters_for;  // (device, smem) -> co-resident pairs
@@ -1027,7 +1110,7 @@ int launchPair(const fpk_gemm_desc_t& d, const Plan& pl, const CUtensorMap& map_
   cfg.gridDim = dim3(2 * (tiles < clusters ? tiles : clusters));
   cfg.numAttrs = 2;
   prof::countLaunch(prof::kGemm);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN, MH>, d, pl, map_w, map_a, map_a_tail);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemmPairKernel<T, BN, MH>, d, pl, map_w, map_a, map_a_tail, map_out);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(std::string("gemmPairKernel launch: ") + cudaGetErrorString(e));
@@ -1152,6 +1235,11 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
     // For 1x1 layers the weight order does not depend on the chunk width
     // (k' = channel), so wider windows (fewer activation barriers per MMA) are
     // free to choose; the widest that keeps the pipeline as deep is taken.
+    // Dense 16-bit outputs (the transformer linears: SAME layout, every row
+    // valid) leave the epilogue as TMA bulk stores of staged 32-column chunks.
+    const bool tma_store = g_tma_store.load() && esize == 2 && bn == 256 && d.dst_mode == FPK_DST_SAME &&
+                           d.grid_w == 1 && d.valid_w >= 1 && d.valid_h >= d.img_rows;
+    const size_t stage_reserve = tma_store ? kOutStageBytes + 1024 : 0;
     Plan pp = pl;
     pp.win_rows = pair_mh * kBlockM + (mx - mn);
     pp.b_stage_bytes = static_cast<uint32_t>(bn / 2) * 128u;
@@ -1174,7 +1262,9 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
       c.a_plane_pitch = c.win_rows <= 128 ? static_cast<uint32_t>(c.win_rows * 16)
                                           : (static_cast<uint32_t>(c.win_rows * 16) + 127u) & ~127u;
       c.a_slot_bytes = (static_cast<uint32_t>(c.planes) * c.a_plane_pitch + 1023u) & ~1023u;
-      if (!chooseSlots(c.a_slot_bytes, c.b_stage_bytes, c.stages_per_chunk, &c.a_slots, &c.b_stages)) continue;
+      if (!chooseSlots(c.a_slot_bytes, c.b_stage_bytes, c.stages_per_chunk, &c.a_slots, &c.b_stages, stage_reserve)) {
+        continue;
+      }
       const int depth = c.a_slots * c.stages_per_chunk < c.b_stages ? c.a_slots * c.stages_per_chunk : c.b_stages;
       if (depth >= best_depth) {
         best_depth = depth;
@@ -1183,10 +1273,21 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
       }
     }
     if (planned && pp.m_tiles * pp.n_tiles >= numSms() / 2) {
-      const size_t smem = 1024 + static_cast<size_t>(pp.b_stages) * pp.b_stage_bytes +
-                          static_cast<size_t>(pp.a_slots) * pp.a_slot_bytes + sizeof(Smem);
+      size_t smem = 1024 + static_cast<size_t>(pp.b_stages) * pp.b_stage_bytes +
+                    static_cast<size_t>(pp.a_slots) * pp.a_slot_bytes + sizeof(Smem);
+      pp.tma_store = tma_store ? 1 : 0;
+      pp.stage_off = 0;
+      if (tma_store) {
+        pp.stage_off = static_cast<uint32_t>((smem - 1024 + 1023) & ~static_cast<size_t>(1023));
+        smem = 1024 + pp.stage_off + kOutStageBytes;
+      }
       CUtensorMap map_w, map_a;
       if (makeWeightMap(d, kprime, bn / 2, &map_w) != 0) return 1;
+      CUtensorMap map_out = map_w;  // unused unless tma_store
+      if (tma_store && makePlanarRowsMap(d.dst, d.rows, d.cout / 8, d.dst_plane_stride, 32, 4, &map_out,
+                                         "fpk_gemm (output)") != 0) {
+        return 1;
+      }
       CUtensorMap map_a_tail;
       const int total_planes = d.cin * esize / 16;
       if (pp.win_rows <= 128) {
@@ -1204,18 +1305,18 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
       }
       switch (d.dtype) {
         case FPK_DTYPE_BF16:
-          return bn == 256   ? launchPair<__nv_bfloat16, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                 : bn == 128 ? launchPair<__nv_bfloat16, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                             : launchPair<__nv_bfloat16, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256   ? launchPair<__nv_bfloat16, 256, 1>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s)
+                 : bn == 128 ? launchPair<__nv_bfloat16, 128, 2>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s)
+                             : launchPair<__nv_bfloat16, 64, 2>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s);
         case FPK_DTYPE_F32:
         case FPK_DTYPE_F32_EXACT:
-          return bn == 256   ? launchPair<float, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                 : bn == 128 ? launchPair<float, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                             : launchPair<float, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256   ? launchPair<float, 256, 1>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s)
+                 : bn == 128 ? launchPair<float, 128, 2>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s)
+                             : launchPair<float, 64, 2>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s);
         default:
-          return bn == 256   ? launchPair<__half, 256, 1>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                 : bn == 128 ? launchPair<__half, 128, 2>(d, pp, map_w, map_a, map_a_tail, smem, s)
-                             : launchPair<__half, 64, 2>(d, pp, map_w, map_a, map_a_tail, smem, s);
+          return bn == 256   ? launchPair<__half, 256, 1>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s)
+                 : bn == 128 ? launchPair<__half, 128, 2>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s)
+                             : launchPair<__half, 64, 2>(d, pp, map_w, map_a, map_a_tail, map_out, smem, s);
       }
     }
   }
@@ -1262,6 +1363,10 @@ extern "C" int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream) {
 
 extern "C" int fpk_gemm_set_cta_pairs(int enable) {
   return fpb::gemm::g_cta_pairs.exchange(enable != 0) ? 1 : 0;
+}
+
+extern "C" int fpk_gemm_set_tma_store(int enable) {
+  return fpb::gemm::g_tma_store.exchange(enable != 0) ? 1 : 0;
 }
 
 extern "C" int fpk_gemm_test_withhold_loads(int enable) {

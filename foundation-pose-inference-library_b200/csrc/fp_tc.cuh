@@ -305,5 +305,22 @@ __device__ __forceinline__ void fenceProxyAsyncSmem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Bulk tensor store of a shared-memory tile to global memory (this GPU's own
+// memory, no multicast), tracked in the issuing thread's bulk groups. c0 is
+// the innermost coordinate: c0 x element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tmaStore2d(const CUtensorMap* map, int c0, int c1, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(c0),
+               "r"(c1), "r"(smemU32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulkCommit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulkWaitRead() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until every committed group has completed (its writes performed).
+__device__ __forceinline__ void bulkWaitAll() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 }  // namespace tc
 }  // namespace fpb

@@ -70,6 +70,7 @@ _SIGS = {
     "fpk_select_best": (C.c_int, [_P, _P, C.c_int, C.POINTER(C.c_float), _P, _P]),
     "fpk_gemm": (C.c_int, [_P, _P]),
     "fpk_gemm_set_cta_pairs": (C.c_int, [C.c_int]),
+    "fpk_gemm_set_tma_store": (C.c_int, [C.c_int]),
     "fpk_gemm_test_withhold_loads": (C.c_int, [C.c_int]),
     "fpk_attention": (C.c_int, [_P, C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_int, _P, C.c_longlong,
                                 C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),

@@ -243,6 +243,14 @@ FP_API int fpk_gemm(const fpk_gemm_desc_t* desc, void* stream);
  * returns the previous setting. No reference counterpart (a tuning switch). */
 FP_API int fpk_gemm_set_cta_pairs(int enable);
 
+/* Tuning switch (no reference counterpart): with enable != 0 (the default),
+ * dense 16-bit layers on CTA pairs (SAME destination, every row valid, 256-
+ * channel tiles: the transformer linears) stage each 32-column chunk of the
+ * output in shared memory and write it with one bulk tensor store per warp;
+ * enable = 0 keeps per-thread 16-byte stores. Results are bit-identical either
+ * way. Process-wide; returns the previous setting. */
+FP_API int fpk_gemm_set_tma_store(int enable);
+
 /* Failure-injection test switch (no reference counterpart). With enable != 0
  * every following fpk_gemm runs on single-CTA tiles whose producer issues no
  * loads, so the MMA warp's bounded wait for its first operand tile runs out

@@ -312,6 +312,44 @@ def test_pair_tiles_equal_single_tiles(fpk, err, dtype, cout, cin):
     assert torch.equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("rows,cin,cout,dtype,res,relu", [(100800, 512, 1536, FPK_DTYPE_F16, False, False),
+                                                          (100800, 512, 512, FPK_DTYPE_F16, True, False),
+                                                          (40000, 512, 512, FPK_DTYPE_BF16, False, True),
+                                                          # ragged last pair tile: rows past the end clipped
+                                                          (37001, 256, 256, FPK_DTYPE_BF16, True, True)])
+def test_staged_stores_equal_thread_stores(fpk, err, rows, cin, cout, dtype, res, relu):
+    """Dense 16-bit layers on CTA pairs leave the epilogue as bulk tensor stores
+    of staged 32-column chunks: the same bits as per-thread stores, against
+    torch, and nothing written outside the layer's rows (guard rows stay 0)."""
+    g = torch.Generator().manual_seed(rows + cout)
+    dt = DT[dtype]
+    A = torch.randn(rows, cin, generator=g)
+    W = torch.randn(cout, cin, generator=g) / math.sqrt(cin)
+    b = torch.randn(cout, generator=g).to(DEV)
+    pa = Planar(rows, cin, dt).set(A.to(DEV))
+    w = chunk_major(W.reshape(cout, 1, cin), dtype).to(dt).to(DEV)
+    pr = Planar(rows, cout, dt).set(torch.randn(rows, cout, generator=g).to(DEV)) if res else None
+    outs = []
+    for staged in (1, 0):
+        prev = fpk.lib.fpk_gemm_set_tma_store(staged)
+        try:
+            out = Planar(rows, cout, dt)
+            gemm(fpk, make_desc(pa, rows, cin, [0], w, cout, out, dtype, err, bias=b, residual=pr, relu=relu))
+            torch.cuda.synchronize()
+        finally:
+            fpk.lib.fpk_gemm_set_tma_store(prev)
+        assert err.item() == 0
+        assert torch.count_nonzero(out.t[:, :256]) == 0 and torch.count_nonzero(out.t[:, 256 + rows:]) == 0
+        outs.append(out.get())
+    assert torch.equal(outs[0], outs[1])
+    ref = A.to(dt).float().to(DEV) @ W.to(dt).float().to(DEV).T + b
+    if res:
+        ref = ref + pr.get().float()
+    if relu:
+        ref = torch.relu(ref)
+    close(outs[0], ref)
+
+
 # Split K (tracking one hypothesis): few output tiles, so each tile's K range
 # is split over several CTAs whose fp32 partial sums a second launch adds in
 # split order. Checked against torch, against the unsplit kernel, and for
