@@ -627,7 +627,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tcCommitElect(&sm->a_empty[slot]);
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
         }
-        tcCommitElect(&sm->acc_full[buf]);
+        // A tile whose operand wait gave up is never handed to the epilogue:
+        // its warps see the error flag and exit without storing.
+        if (ok) tcCommitElect(&sm->acc_full[buf]);
       }
       // Drain: wait until every MMA issued above has completed (also after an
       // error: TMEM is released only once no MMA can still write it).
@@ -899,7 +901,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tcCommitPairBothElect(&sm->a_empty[slot]);
           if (++slot == pl.a_slots) { slot = 0; a_phase ^= 1; }
         }
-        tcCommitPairBothElect(&sm->acc_full[buf]);
+        if (ok) tcCommitPairBothElect(&sm->acc_full[buf]);  // as in gemmKernel: no partial tile is stored
       }
       tcCommitPairOwnElect(&sm->drain);
       drainBar(&sm->drain, 0);  // as in gemmKernel: no MMA in flight past this point
