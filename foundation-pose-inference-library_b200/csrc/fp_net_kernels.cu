@@ -144,13 +144,13 @@ __device__ __forceinline__ uint32_t fromF2<__nv_bfloat16>(float lo, float hi) {
 }
 
 // LayerNorm over 512 channels of 16-bit planar activations, in registers: a
-// warp normalises 8 rows; lane l holds channel planes g, g+4, ..., g+60
-// (g = l / 8) of row l % 8, so every warp-wide load or store moves 4 planes x
-// 8 consecutive rows (128 contiguous bytes, a whole line, per plane), and all
-// 16 loads of a lane are in flight together. Row statistics: per-lane partial
-// sums, then a butterfly over the 4 lanes of the row.
+// warp normalises 4 rows; lane l holds channel planes g, g+8, ..., g+56
+// (g = l / 4) of row l % 4, so every warp-wide load or store moves 8 planes x
+// 4 consecutive rows (64 contiguous bytes per plane), and all 8 loads of a
+// lane are in flight together. Row statistics: per-lane partial sums, then a
+// butterfly over the 8 lanes of the row.
 template <typename T>
-__global__ void __launch_bounds__(256, 1) layerNorm16Kernel(LnArgs a) {
+__global__ void __launch_bounds__(256, 2) layerNorm16Kernel(LnArgs a) {
   tc::pdlTrigger();
   __shared__ float gamma[512], beta[512];
   for (int i = threadIdx.x; i < 512; i += 256) {
@@ -159,21 +159,20 @@ __global__ void __launch_bounds__(256, 1) layerNorm16Kernel(LnArgs a) {
   }
   __syncthreads();
   tc::pdlWait();  // weights above; activations from here on
-  constexpr int kRec = 16;  // records (planes) per lane
   const int lane = threadIdx.x & 31;
-  const int g = lane >> 3;
-  const long long row = (static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * 8 + (lane & 7);
+  const int g = lane >> 2;
+  const long long row = (static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * 4 + (lane & 3);
   const bool valid = row < a.rows;
-  uint4 rec[kRec];
+  uint4 rec[8];
 #pragma unroll
-  for (int k = 0; k < kRec; ++k) {
-    rec[k] = valid ? *reinterpret_cast<const uint4*>(a.in + static_cast<long long>(g + 4 * k) * a.in_plane_stride +
+  for (int k = 0; k < 8; ++k) {
+    rec[k] = valid ? *reinterpret_cast<const uint4*>(a.in + static_cast<long long>(g + 8 * k) * a.in_plane_stride +
                                                      row * 16)
                    : make_uint4(0, 0, 0, 0);
   }
   float s = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kRec; ++k) {
+  for (int k = 0; k < 8; ++k) {
     const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -181,12 +180,12 @@ __global__ void __launch_bounds__(256, 1) layerNorm16Kernel(LnArgs a) {
       s += f.x + f.y;
     }
   }
-  s += __shfl_xor_sync(0xffffffffu, s, 8);
-  s += __shfl_xor_sync(0xffffffffu, s, 16);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   const float mean = s * (1.0f / 512.0f);
   float q = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kRec; ++k) {
+  for (int k = 0; k < 8; ++k) {
     const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -196,13 +195,13 @@ __global__ void __launch_bounds__(256, 1) layerNorm16Kernel(LnArgs a) {
       q += d0 * d0 + d1 * d1;
     }
   }
-  q += __shfl_xor_sync(0xffffffffu, q, 8);
-  q += __shfl_xor_sync(0xffffffffu, q, 16);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
   const float rstd = rsqrtf(q * (1.0f / 512.0f) + a.eps);
   if (!valid) return;
 #pragma unroll
-  for (int k = 0; k < kRec; ++k) {
-    const int ch = (g + 4 * k) * 8;
+  for (int k = 0; k < 8; ++k) {
+    const int ch = (g + 8 * k) * 8;
     const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
     uint32_t o[4];
 #pragma unroll
@@ -211,7 +210,7 @@ __global__ void __launch_bounds__(256, 1) layerNorm16Kernel(LnArgs a) {
       const int c = ch + 2 * j;
       o[j] = fromF2<T>((f.x - mean) * rstd * gamma[c] + beta[c], (f.y - mean) * rstd * gamma[c + 1] + beta[c + 1]);
     }
-    *reinterpret_cast<uint4*>(a.out + static_cast<long long>(g + 4 * k) * a.out_plane_stride + row * 16) =
+    *reinterpret_cast<uint4*>(a.out + static_cast<long long>(g + 8 * k) * a.out_plane_stride + row * 16) =
         make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
@@ -463,14 +462,14 @@ cudaError_t launchLayerNorm(const LnArgs& a, int dtype, cudaStream_t s) {
   prof::Scope scope(prof::kOther, 0.0, s);
   switch (dtype) {
     case FPK_DTYPE_BF16:
-      return launchPdl(layerNorm16Kernel<__nv_bfloat16>, dim3(static_cast<unsigned>((a.rows + 63) / 64)), dim3(256), 0, s, a);
+      return launchPdl(layerNorm16Kernel<__nv_bfloat16>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
     case FPK_DTYPE_F32:
       return launchPdl(layerNormKernel<float, 16>, dim3(static_cast<unsigned>((a.rows + 15) / 16)), dim3(256), 0, s, a);
     case FPK_DTYPE_F32_EXACT:
       return launchPdl(layerNormKernel<float, 16, true>, dim3(static_cast<unsigned>((a.rows + 15) / 16)), dim3(256), 0,
                        s, a);
     default:
-      return launchPdl(layerNorm16Kernel<__half>, dim3(static_cast<unsigned>((a.rows + 63) / 64)), dim3(256), 0, s, a);
+      return launchPdl(layerNorm16Kernel<__half>, dim3(static_cast<unsigned>((a.rows + 31) / 32)), dim3(256), 0, s, a);
   }
 }
 
