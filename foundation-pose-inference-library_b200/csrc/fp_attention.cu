@@ -445,6 +445,9 @@ __global__ void __launch_bounds__(Geo<T>::kThreads, Geo<T>::kMinBlocks)
       if (lane == 0) mbarArrive(&bars->p_full);
     }
     if (ok) ok = waitBar(&bars->o_done, 0, err, 30);
+    // The MMA warp also signals o_done when it gave up part-way (it drains on
+    // that barrier): after any reported error O is not stored.
+    if (ok && *reinterpret_cast<volatile int*>(err) != 0) ok = false;
     if (ok) {
       tcFenceAfter();
       const float inv = 1.0f / l;
